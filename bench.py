@@ -1,0 +1,403 @@
+#!/usr/bin/env python
+"""bench.py — BitNet-2B decode throughput on B200 (bitnetrs hot path).
+
+Default workload (BASELINE config "continuous-batching decode"): the 2B
+architecture with random-init weights (N(0,0.02), absmean-ternarised, packed
+in the reference format), 256 concurrent sequences per GPU whose contexts are
+seeded with lengths U[128, 4096] and N(0,1) bf16 K/V, greedy decode.  A step
+is one decode step of all 256 sequences.  Data parallel: every rank owns its
+own 256 sequences and a full weight replica; there is no collective on the
+data path ("scaling": "weak").
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+`value` is device-timed (CUDA events on the launching stream, max over ranks)
+with weights, KV and tokens resident in HBM; `e2e` is the same metric through
+the host-buffer C-ABI call bitnet_cuda_decode_step (token ids in from host,
+next-token ids out to host every step).  `--impl reference` times the CPU
+restatement of the reference backend (oracle/) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s (BitNet-2B shape, batch 1 & 256) at 1/2/4/8 B200; ternary GEMV HBM GB/s"
+CTX_LO, CTX_HI = 128, 4096
+SEED = 0
+E2E_STEPS = 8
+
+
+def args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def model_config():
+    from bitnetrs_b200 import bitnet_2b_config
+
+    cfg = bitnet_2b_config()
+    # Contexts reach 4096 + decode steps, past the 2B model's 4096; RoPE is
+    # defined for any position (the reference rebuilds its cache), so the
+    # benchmark model accepts 4096 + 512 positions.
+    cfg.max_position_embeddings = CTX_HI + 512
+    return cfg
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles(name):
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get(name)
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle (restatement of the reference CPU backend)
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(weights, cfg, ctxs, rank_seed, budget_s=15.0, max_tokens=32, warm=1):
+    """Greedy-decode tokens on seeded contexts with the oracle; returns (tok/s, tokens, seconds, threads)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as O
+    from bitnetrs_b200 import synth
+
+    om = O.OracleModel(weights)
+    kvs, toks = [], []
+    for i, n in enumerate(ctxs):
+        kv = om.kv(n + max_tokens + warm + 2, bf16=True)
+        k, v = synth.kv_normal(rank_seed, i, cfg, n)
+        kv.seed(k, v)
+        kvs.append((kv, n))
+        toks.append(int(synth.uniform_u32(rank_seed, 3, len(ctxs), 0, cfg.vocab_size - 1)[i]))
+    pos = [n for _, n in kvs]
+    L = O.lib()
+    for _ in range(warm):
+        for i, (kv, _) in enumerate(kvs):
+            lg = om.forward(kv, [toks[i]], pos[i])
+            toks[i] = L.orc_greedy_argmax(O.p(lg), lg.size)
+            pos[i] += 1
+    done, t0 = 0, time.perf_counter()
+    while done < max_tokens and (time.perf_counter() - t0) < budget_s:
+        for i, (kv, _) in enumerate(kvs):
+            lg = om.forward(kv, [toks[i]], pos[i])
+            toks[i] = L.orc_greedy_argmax(O.p(lg), lg.size)
+            pos[i] += 1
+            done += 1
+    dt = time.perf_counter() - t0
+    return done / dt, done, dt, int(L.orc_threads())
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from bitnetrs_b200 import synth
+
+    cfg = model_config()
+    weights = synth.random_model(cfg, seed=SEED)
+    ctxs = synth.uniform_u32(SEED, 11, 2, CTX_LO, CTX_HI).tolist()
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as O
+
+    om = O.OracleModel(weights)
+    kvs, toks, pos = [], [], []
+    for i, n in enumerate(ctxs):
+        kv = om.kv(n + a.steps + a.warmup + 2, bf16=True)
+        k, v = synth.kv_normal(SEED, i, cfg, n)
+        kv.seed(k, v)
+        kvs.append(kv)
+        pos.append(n)
+        toks.append(int(synth.uniform_u32(SEED, 3, 2, 0, cfg.vocab_size - 1)[i]))
+    L = O.lib()
+
+    def step():
+        for i, kv in enumerate(kvs):
+            lg = om.forward(kv, [toks[i]], pos[i])
+            toks[i] = L.orc_greedy_argmax(O.p(lg), lg.size)
+            pos[i] += 1
+
+    for _ in range(a.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step()
+    dt = time.perf_counter() - t0
+    v = len(kvs) * a.steps / dt
+    sample = (f"{len(kvs)} sequences (contexts {ctxs}) x {a.steps} greedy decode steps, sequence-serial "
+              "like the reference (one engine per sequence)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i2xi8->i32, f32 KV (bf16-rounded values)", "data": "synthetic",
+        "config": {"workload": "C4 continuous-batching decode, BitNet-2B shape (CPU sample)",
+                   "ctx": f"U[{CTX_LO},{CTX_HI}] seeded", "parallelism": "host threads"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": int(L.orc_threads()), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+def run_cuda(a):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, kernel_launches, synth
+
+    B, K, W = a.batch, a.steps, a.warmup
+    cfg = model_config()
+    t_setup = time.perf_counter()
+    weights = synth.random_model(cfg, seed=SEED)
+    backend = CudaBackend(local)
+    model = BitNetModel(weights, backend, max_batch_tokens=max(B, 256))
+    rank_seed = SEED + 1000 * rank
+    ctxs = synth.uniform_u32(rank_seed, 11, B, CTX_LO, CTX_HI).astype(np.int64)
+    total_steps = W + K + 3 + E2E_STEPS + 2
+    pages = int(np.sum((ctxs + total_steps + 15) // 16)) + 64 + (128 + 64 + 15) // 16
+    kv = model.new_kv_cache(num_pages=pages, max_seqs=B + 1, kv_dtype=KV_BF16)
+    for i in range(B):
+        kv.fill_random(i, int(ctxs[i]), rank_seed)
+        kv.reserve(i, int(ctxs[i]) + total_steps)
+    seqs = np.arange(B, dtype=np.uint32)
+    dev = torch.device("cuda", local)
+    tok0 = synth.uniform_u32(rank_seed, 3, B, 0, cfg.vocab_size - 1)
+    d_tok = torch.tensor(tok0.astype(np.int64), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t_setup
+
+    def step():
+        model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            step()
+    torch.cuda.synchronize()
+    model.check()
+
+    # ---- timed region: K device-resident decode steps ----
+    clocks = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.25)  # at least one sample before load
+    launches0 = kernel_launches()
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(K):
+            step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = kernel_launches() - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    model.check()
+    ms_per_step = ms / K
+    value = world * B * K / (ms / 1e3)
+
+    # ---- per-kernel device time (CUDA events recorded inside the decode graph) ----
+    model.set_kernel_timing(True)
+    ctx_before = np.array([kv.len(i) for i in range(B)], dtype=np.int64)
+    with torch.cuda.stream(stream):
+        step()  # capture + run
+        step()
+    torch.cuda.synchronize()
+    kt = model.kernel_times()
+    model.set_kernel_timing(False)
+    # attention reads every cached K/V position (bf16) once per layer + q in / out
+    L, nkv, hd, H = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim(), cfg.hidden_size
+    ctx_at = ctx_before + 2  # positions attended in the last timed step (incl. its own token)
+    attn_bytes = float(np.sum(ctx_at) * nkv * hd * 2 * 2 + 2 * B * H * 4)
+    attn_ms, attn_n = kt["attention"]
+    attn_launch_ms = attn_ms / max(attn_n, 1) * 1.0
+    attn_gbs = attn_bytes / (attn_launch_ms / 1e3) / 1e9 if attn_n else None
+    peak, peak_kind = peaks()
+    # ternary matmul: weight stream per step + int8 activations + f32 outputs
+    qd, kvd, F = cfg.q_dim(), cfg.kv_dim(), cfg.intermediate_size
+    w_bytes = L * ((qd + 2 * kvd) * H + H * qd + 2 * F * H + H * F) / 4
+    act_bytes = L * B * ((H + qd + H + F) + 4 * ((qd + 2 * kvd) + H + 2 * F + H))
+    mm_ms, mm_n = kt["ternary_matmul"]
+    mm_ops = 2.0 * B * L * ((qd + 2 * kvd) * H + H * qd + 2 * F * H + H * F)
+
+    # ---- e2e: host token ids in / out through bitnet_cuda_decode_step ----
+    host_tok = d_tok.cpu().numpy().astype(np.uint32)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(E2E_STEPS):
+        host_tok, _ = model.decode_step(kv, seqs, host_tok)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * B * E2E_STEPS / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(B * 4 + B * 8), "d2h_bytes_per_step": int(B * 4),
+           "api": "bitnet_cuda_decode_step (host token ids in, greedy next ids out)", "steps": E2E_STEPS}
+
+    # ---- batch-1 decode (BASELINE's batch-1 number), same model ----
+    b1 = None
+    s1 = B  # spare sequence slot
+    kv.fill_random(s1, 128, rank_seed + 7)
+    kv.reserve(s1, 128 + 40)
+    d1 = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            model.decode_step_device(kv, [s1], d1.data_ptr(), d1.data_ptr(), 0, stream.cuda_stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(32):
+            model.decode_step_device(kv, [s1], d1.data_ptr(), d1.data_ptr(), 0, stream.cuda_stream)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    b1_ms = e0.elapsed_time(e1) / 32
+    b1 = {"value": 1e3 / b1_ms, "unit": "tokens/s", "ms_per_token": b1_ms, "context": "128..160"}
+    model.check()
+
+    # ---- CPU baseline (rank 0, N=1) ----
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        ctx_sample = [int(c) for c in ctxs[:2]]
+        v, n, dt, thr = cpu_decode_sample(weights, cfg, ctx_sample, rank_seed)
+        cpu = {"value": v, "unit": "tokens/s", "cores": thr, "kind": "port",
+               "sample": f"{n} greedy decode tokens over 2 of the seeded sequences (contexts {ctx_sample}), "
+                         f"sequence-serial like the reference, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "i2xi8->i32 matmul, f32 norm/attention, bf16 KV",
+            "data": "synthetic: random-init 2B weights N(0,0.02) absmean-ternarised; contexts U[128,4096] "
+                    "seeded with N(0,1) bf16 K/V",
+            "config": {"workload": "C4 continuous-batching decode, BitNet-2B shape", "batch_per_gpu": B,
+                       "global_batch": B * world, "ctx": f"U[{CTX_LO},{CTX_HI}] seeded per rank",
+                       "kv": "paged bf16, 16-token pages", "parallelism": f"dp{world} (replicated weights, no "
+                                                                         f"collective)",
+                       "l2": "inputs larger than L2 (~44 GB of KV read per step)"},
+            "e2e": e2e,
+            "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel (decode, split-K)",
+                         "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": (attn_gbs / peak) if attn_gbs else None,
+                         "traffic": traffic_from_profiles("paged_attention_kernel"),
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": attn_bytes,
+                         "avg_launch_ms": attn_launch_ms},
+            "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32, mma.sync)", "ms_per_step": mm_ms,
+                     "launches": mm_n, "hbm_gbs": (w_bytes + act_bytes) / (mm_ms / 1e3) / 1e9 if mm_ms else None,
+                     "tops": mm_ops / (mm_ms / 1e3) / 1e12 if mm_ms else None},
+            "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kt.items()},
+            "batch1": b1,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": int(launches),
+            "setup_s": round(setup_s, 1),
+        }
+        print(json.dumps(line), flush=True)
+    kv.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = args()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_cuda(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

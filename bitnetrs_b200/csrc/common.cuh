@@ -1,0 +1,117 @@
+// common.cuh — shared helpers for the bitnetrs B200 backend.
+//
+// Numerics: every translation unit is compiled with -fmad=false, so a*b+c is
+// two IEEE roundings unless __fmaf_rn is written explicitly.  This is what
+// makes the kernels bit-identical to the reference's CPU code, where scalar
+// Rust never contracts and FMA only appears through _mm256_fmadd_ps.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/bitnet_cuda.h"
+
+namespace bitnet {
+
+// ---------------------------------------------------------------------------
+// Host-side error reporting (thread-local last error, BitNetError codes).
+// ---------------------------------------------------------------------------
+void set_error(int code, const char* fmt, ...);
+int shape_error(const std::string& expected, const std::string& got);
+int quant_error(const std::string& msg);
+int config_error(const std::string& msg);
+int backend_error(const std::string& msg);
+int cuda_error(cudaError_t e, const char* what);
+
+#define BN_CUDA(call)                                  \
+  do {                                                 \
+    cudaError_t _e = (call);                           \
+    if (_e != cudaSuccess) return cuda_error(_e, #call); \
+  } while (0)
+
+#define BN_TRY(call)          \
+  do {                        \
+    int _rc = (call);         \
+    if (_rc != BITNET_OK) return _rc; \
+  } while (0)
+
+inline size_t round_up(size_t x, size_t m) { return (x + m - 1) / m * m; }
+inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
+
+// Device layout of one ternary tensor [rows, cols]: each row is padded to a
+// multiple of 64 columns (16 bytes) and stored as 32-bit words of 16 codes.
+// Code c in {0,1,2} stands for the weight 1-c (+1, 0, -1), as in the
+// reference format (ternary.rs:266-285); the reference's invalid code 3 is
+// rewritten to 1 (zero) at upload, matching DECODE_LUT (simd.rs:390-405).
+// Inside a word, element e = 4*i + j of the 16 lives in byte j, bits 2i..2i+1,
+// so (word >> 2i) & 0x03030303 yields the codes of elements 4i..4i+3 as four
+// consecutive bytes — ready for dp4a / int8 MMA without a lookup table.
+inline size_t padded_cols(size_t cols) { return round_up(cols, 64); }
+inline size_t words_per_row(size_t cols) { return padded_cols(cols) / 16; }
+
+// ---------------------------------------------------------------------------
+// Device helpers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// half::bf16::from_f32: round to nearest even, NaN kept quiet.
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u | 0x00400000u) >> 16);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// The reference's hsum_f32_avx2 (simd.rs:292-307) over eight lane sums:
+// ((a0+a4) + (a1+a5)) + ((a2+a6) + (a3+a7)).
+__device__ __forceinline__ float hsum8(const float a[8]) {
+  float s0 = __fadd_rn(a[0], a[4]);
+  float s1 = __fadd_rn(a[1], a[5]);
+  float s2 = __fadd_rn(a[2], a[6]);
+  float s3 = __fadd_rn(a[3], a[7]);
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reductions for blockDim.x a multiple of 32 (<= 1024).
+template <class T, class Op>
+__device__ __forceinline__ T block_reduce(T v, Op op, T* smem32) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) smem32[warp] = v;
+  __syncthreads();
+  T r = smem32[0];
+  for (int i = 1; i < nw; ++i) r = op(r, smem32[i]);
+  return r;
+}
+
+// Rust f32::round: half away from zero (roundf), then clamp, then cast.
+__device__ __forceinline__ int8_t quant_i8(float x, float inv) {
+  float s = roundf(__fmul_rn(x, inv));
+  s = fminf(fmaxf(s, -128.0f), 127.0f);
+  return (int8_t)(int)s;
+}
+
+}  // namespace bitnet

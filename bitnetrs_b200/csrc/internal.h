@@ -1,0 +1,56 @@
+// internal.h — host-side structures shared by the C-ABI translation units.
+#pragma once
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+
+namespace bitnet {
+
+// Grow-only device buffer.
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  int ensure(size_t bytes);
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+  void release();
+  ~DevBuf() { release(); }
+};
+
+// RoPE table with the reuse rule of CpuBackend::rope_embed (cpu/src/lib.rs:289-314):
+// rebuilt when head_dim changes, theta moves by more than 1e-3, or pos >= max_seq.
+struct RopeTable {
+  bool valid = false;
+  size_t head_dim = 0, max_seq = 0;
+  float theta = 0.0f;
+  std::vector<float> cos, sin;  // [max_seq][head_dim/2], glibc powf/cosf/sinf
+  DevBuf d_cos, d_sin;
+};
+
+// Fill cos/sin for positions [0, max_seq) exactly as RopeCache::new (rope.rs:100-147).
+int build_rope_host(size_t max_seq, size_t head_dim, float theta, std::vector<float>& cos, std::vector<float>& sin);
+
+}  // namespace bitnet
+
+struct bitnet_cuda_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  std::string name;
+  bitnet::DevBuf b[8];  // scratch for the per-call trait methods
+  bitnet::DevBuf status;
+  bitnet::RopeTable rope;
+};
+
+struct bitnet_cuda_weight {
+  bitnet_cuda_ctx* ctx = nullptr;
+  int rows = 0, cols = 0;
+  float scale = 0.0f;
+  uint32_t* words = nullptr;
+};

@@ -1,0 +1,115 @@
+// kernels.cuh — launchers for the device kernels (all asynchronous on `st`).
+#pragma once
+
+#include "common.cuh"
+
+namespace bitnet {
+
+// Per-launch kernel counter (reported by bitnet_cuda_kernel_launches).
+void count_launch(uint64_t n = 1);
+void uncount_launch(uint64_t n);
+uint64_t launches_total();
+
+// ---- weight layout ----------------------------------------------------------
+// Reference 2-bit rows [rows][ceil(cols/4)] -> device words [rows][words_per_row(cols)].
+void launch_repack_ternary(const uint8_t* src, uint32_t* dst, int rows, int cols, cudaStream_t st);
+
+// ---- activation quantisation / norms ---------------------------------------
+// absmax_quantize_row_into per row.  x: [M][ldx] (f32, or bf16 bits when x_bf16).
+// xq: [M][ldq] zero padded to ldq; act_absmax[m] = (mc/127)*127; scale[m] = mc/127
+// (either may be null); row_sum[m] = sum of xq; status |= 1 on non-finite input.
+void launch_quantize_rows(const void* x, bool x_bf16, int ldx, int M, int K, int8_t* xq, int ldq, float* act_absmax,
+                          float* scale, int32_t* row_sum, int32_t* status, cudaStream_t st);
+
+// rms_norm in the reference order (norm.rs:113-137): out[m] = (x*inv)*w.
+void launch_rms_norm(const float* x, int ldx, const float* w, int d, float eps, float* out, int ldo, int M,
+                     cudaStream_t st);
+
+// rms_norm followed by absmax quantisation of the normalised row (the model's
+// rms_norm -> absmax_quantize_row_into pairs, model/src/lib.rs:952-962 etc.).
+// When `gate_up` is set, the row is first formed as sqrelu(gate)*up
+// (simd.rs:1135-1184) from x (gate) and x2 (up).
+void launch_norm_quant(const float* x, const float* x2, int ldx, const float* w, int d, float eps, int8_t* xq, int ldq,
+                       float* act_absmax, int32_t* row_sum, int32_t* status, int M, cudaStream_t st);
+
+// ---- elementwise -------------------------------------------------------------
+void launch_squared_relu(float* x, size_t n, cudaStream_t st);
+void launch_sqrelu_gate(const float* g, const float* u, float* out, size_t n, cudaStream_t st);
+void launch_elementwise_mul(const float* a, const float* b, float* out, size_t n, cudaStream_t st);
+// activation::softmax in place over one vector (sequential sum order).
+void launch_softmax(float* x, size_t n, float* scratch_max, cudaStream_t st);
+// bf16 embedding rows -> f32 hidden rows.
+void launch_embed(const uint16_t* embed, const uint32_t* tokens, int T, int H, float* h, int32_t* status, int vocab,
+                  cudaStream_t st);
+
+// dst[r] = src[rows[r]] for r < n (rows of length ld).
+void launch_gather_rows(const float* src, int ld, const int32_t* rows, int n, float* dst, cudaStream_t st);
+
+// ---- ternary matmul ------------------------------------------------------------
+// Output segments: rows [seg_end[s-1], seg_end[s]) use scale seg_scale[s].
+struct Segments {
+  int n = 1;
+  int end[3] = {0, 0, 0};
+  float scale[3] = {0.f, 0.f, 0.f};
+};
+enum class Epi : int { Store = 0, Residual = 1 };
+// out[m][n] = (sum_k W[n,k] x[m][k]) * ((seg_scale*act_absmax[m])/127); Residual: out += that.
+// acc (optional) receives the int32 sums [M][N] (row stride N).
+void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
+                           const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo,
+                           int32_t* acc, cudaStream_t st);
+// row_sum for callers that quantised elsewhere.
+void launch_row_sum(const int8_t* xq, int ldq, int M, int K, int32_t* row_sum, cudaStream_t st);
+
+// ternary_gemv_f32 (gemv.rs:108-165) in the reference's f32 summation order.
+void launch_ternary_gemv_f32(const uint8_t* packed, int N, int K, float ws, const float* x, float* out,
+                             cudaStream_t st);
+
+// ---- lm_head -------------------------------------------------------------------
+enum class LmW : int { I8 = 0, BF16 = 1, F32 = 2 };
+// out[m][v] = dot(W[v], h[m]) (* scales[v] for I8), reference FMA order.
+void launch_lm_head(const void* W, LmW wt, const float* scales, const float* h, int ldh, int M, int V, int H,
+                    float* out, int ldo, cudaStream_t st);
+// greedy argmax per row (ties -> last index, NaN compares Equal).
+void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cudaStream_t st);
+
+// ---- attention -------------------------------------------------------------------
+// Backend::masked_attention on a head-major cache (attention.rs:97-209).
+void launch_masked_attention_headmajor(const float* q, const float* kc, const float* vc, float* out, int nh, int nkv,
+                                       int hd, int stride, int seq_len, float* scratch, cudaStream_t st);
+
+// Backend::rope_embed on one row [q (nh*hd) | k (nkv*hd)] -> out (same layout).
+void launch_rope_apply(const float* qk, int nh, int nkv, int hd, const float* cos_table, const float* sin_table,
+                       size_t pos, float* out, cudaStream_t st);
+
+// Paged KV cache geometry.
+struct KvGeom {
+  void* pool = nullptr;       // [layers][pages][kv_heads][2][16][hd]
+  int bf16 = 1;               // element type
+  int pages = 0, kv_heads = 0, hd = 0, layers = 0;
+  int max_pages_per_seq = 0;  // page table row length
+};
+constexpr int kPage = 16;
+
+// Rotate q/k of T tokens (qkv rows [q | k | v]) with the rope table
+// [max_pos][hd/2] (cos, sin), write rotated q into q_out [T][q_dim] and k/v
+// into the paged cache of `layer` at each token's position.
+void launch_rope_kv_store(const float* qkv, int ldqkv, int T, int nh, int nkv, int hd, const float* rope_cos,
+                          const float* rope_sin, const int32_t* tok_pos, const int32_t* tok_seq,
+                          const int32_t* page_table, const KvGeom& kv, int layer, float* q_out, cudaStream_t st);
+
+// Decode / prefill attention for T query tokens over the paged cache: token t
+// attends to positions [0, tok_pos[t]] of its sequence.
+void launch_paged_attention(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
+                            const int32_t* page_table, const KvGeom& kv, int layer, int max_ctx, float* out,
+                            float* partial, size_t partial_floats, cudaStream_t st);
+size_t paged_attention_partial_floats(int T, int nh, int hd, int max_ctx);
+
+// Fill positions [0, n) of sequence `seq` (all layers) with seeded N(0,1).
+void launch_kv_fill_random(const KvGeom& kv, const int32_t* page_row, int n, uint64_t seed, uint32_t seq,
+                           cudaStream_t st);
+// Copy positions [0,n) between a host-layout staging buffer [layer][pos][kvh*hd] (f32) and the cache.
+void launch_kv_copy(const KvGeom& kv, const int32_t* page_row, int n, float* k_stage, float* v_stage, bool to_cache,
+                    cudaStream_t st);
+
+}  // namespace bitnet

@@ -1,0 +1,298 @@
+// kernels_elem.cu — weight repack, activation quantisation, RMSNorm and the
+// elementwise ops of the bitnetrs hot path.
+#include "kernels.cuh"
+
+#include <atomic>
+
+namespace bitnet {
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+void uncount_launch(uint64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
+uint64_t launches_total() { return g_launches.load(std::memory_order_relaxed); }
+
+// ---------------------------------------------------------------------------
+// Repack (one thread per 32-bit output word).
+// ---------------------------------------------------------------------------
+__global__ void repack_ternary_kernel(const uint8_t* __restrict__ src, uint32_t* __restrict__ dst, int rows, int cols,
+                                      int pc, int kw) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)rows * kw) return;
+  int r = (int)(idx / kw), g = (int)(idx % kw);
+  uint32_t word = 0;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    int k = 16 * g + e;
+    uint32_t code = 1;  // padding columns: weight 0
+    if (k < cols) {
+      code = (src[(size_t)r * pc + (k >> 2)] >> (2 * (k & 3))) & 3u;
+      if (code == 3) code = 1;  // DECODE_LUT maps the invalid code to 0
+    }
+    word |= code << (8 * (e & 3) + 2 * (e >> 2));
+  }
+  dst[idx] = word;
+}
+
+void launch_repack_ternary(const uint8_t* src, uint32_t* dst, int rows, int cols, cudaStream_t st) {
+  int pc = (cols + 3) / 4, kw = (int)words_per_row(cols);
+  size_t n = (size_t)rows * kw;
+  repack_ternary_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(src, dst, rows, cols, pc, kw);
+  count_launch();
+}
+
+// ---------------------------------------------------------------------------
+// absmax quantisation of one row held in shared memory (absmax.rs:127-165).
+// Called by the whole block; y is the row (length d).
+// ---------------------------------------------------------------------------
+__device__ void quantize_row_smem(const float* y, int d, int8_t* xq_row, int ldq, float* act_absmax, float* scale_out,
+                                  int32_t* row_sum, int32_t* status, float* red_f, int* red_i) {
+  float mx = 0.0f;
+  int bad = 0;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float v = y[i];
+    if (!isfinite(v)) bad = 1;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = block_reduce(mx, [](float a, float b) { return fmaxf(a, b); }, red_f);
+  bad = block_reduce(bad, [](int a, int b) { return a | b; }, red_i);
+  float mc = fmaxf(mx, 1e-5f);
+  float scale = __fdiv_rn(mc, 127.0f);
+  float inv = __fdiv_rn(127.0f, mc);
+  int sum = 0;
+  for (int i = threadIdx.x; i < ldq; i += blockDim.x) {
+    int8_t q = 0;
+    if (i < d) q = quant_i8(y[i], inv);
+    xq_row[i] = q;
+    sum += q;
+  }
+  sum = block_reduce(sum, [](int a, int b) { return a + b; }, red_i);
+  if (threadIdx.x == 0) {
+    if (act_absmax) *act_absmax = __fmul_rn(scale, 127.0f);
+    if (scale_out) *scale_out = scale;
+    if (row_sum) *row_sum = sum;
+    if (bad && status) atomicOr(status, 1);
+  }
+}
+
+template <bool BF16>
+__global__ void quantize_rows_kernel(const void* __restrict__ xv, int ldx, int K, int8_t* __restrict__ xq, int ldq,
+                                     float* act_absmax, float* scale, int32_t* row_sum, int32_t* status) {
+  extern __shared__ float row[];
+  __shared__ float red_f[32];
+  __shared__ int red_i[32];
+  int m = blockIdx.x;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    if (BF16)
+      row[i] = bf16_bits_to_f32(((const uint16_t*)xv)[(size_t)m * ldx + i]);
+    else
+      row[i] = ((const float*)xv)[(size_t)m * ldx + i];
+  }
+  __syncthreads();
+  quantize_row_smem(row, K, xq + (size_t)m * ldq, ldq, act_absmax ? act_absmax + m : nullptr,
+                    scale ? scale + m : nullptr, row_sum ? row_sum + m : nullptr, status, red_f, red_i);
+}
+
+void launch_quantize_rows(const void* x, bool x_bf16, int ldx, int M, int K, int8_t* xq, int ldq, float* act_absmax,
+                          float* scale, int32_t* row_sum, int32_t* status, cudaStream_t st) {
+  if (M <= 0) return;
+  size_t smem = (size_t)K * sizeof(float);
+  if (x_bf16)
+    quantize_rows_kernel<true><<<M, 256, smem, st>>>(x, ldx, K, xq, ldq, act_absmax, scale, row_sum, status);
+  else
+    quantize_rows_kernel<false><<<M, 256, smem, st>>>(x, ldx, K, xq, ldq, act_absmax, scale, row_sum, status);
+  count_launch();
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm, reference order (norm.rs:113-137, simd.rs:802-826):
+//   sum_sq = hsum8(8 FMA chains over chunks of 8) + sequential scalar tail
+//   inv = 1 / sqrt(sum_sq / d + eps);  out = (x * inv) * w
+// Lanes 0..7 of warp 0 run the eight chains; the result is broadcast.
+// ---------------------------------------------------------------------------
+__device__ float rms_inv_exact(const float* x, int d, float eps, float* bcast) {
+  if (threadIdx.x < 32) {
+    int lane = threadIdx.x;
+    int chunks = d >> 3;
+    float acc = 0.0f;
+    if (lane < 8) {
+      int i = 0;
+      for (; i + 4 <= chunks; i += 4) {
+        float a0 = x[8 * (i + 0) + lane], a1 = x[8 * (i + 1) + lane];
+        float a2 = x[8 * (i + 2) + lane], a3 = x[8 * (i + 3) + lane];
+        acc = __fmaf_rn(a0, a0, acc);
+        acc = __fmaf_rn(a1, a1, acc);
+        acc = __fmaf_rn(a2, a2, acc);
+        acc = __fmaf_rn(a3, a3, acc);
+      }
+      for (; i < chunks; ++i) {
+        float a = x[8 * i + lane];
+        acc = __fmaf_rn(a, a, acc);
+      }
+    }
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, acc, j);
+    if (lane == 0) {
+      float ss = hsum8(a);
+      for (int i = chunks * 8; i < d; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+      float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps));
+      *bcast = __fdiv_rn(1.0f, rms);
+    }
+  }
+  __syncthreads();
+  return *bcast;
+}
+
+__global__ void rms_norm_kernel(const float* __restrict__ x, int ldx, const float* __restrict__ w, int d, float eps,
+                                float* __restrict__ out, int ldo) {
+  extern __shared__ float row[];
+  __shared__ float bc;
+  int m = blockIdx.x;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) row[i] = x[(size_t)m * ldx + i];
+  __syncthreads();
+  float inv = rms_inv_exact(row, d, eps, &bc);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) out[(size_t)m * ldo + i] = __fmul_rn(__fmul_rn(row[i], inv), w[i]);
+}
+
+void launch_rms_norm(const float* x, int ldx, const float* w, int d, float eps, float* out, int ldo, int M,
+                     cudaStream_t st) {
+  if (M <= 0 || d <= 0) return;
+  rms_norm_kernel<<<M, 256, (size_t)d * sizeof(float), st>>>(x, ldx, w, d, eps, out, ldo);
+  count_launch();
+}
+
+template <bool GATE_UP>
+__global__ void norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ x2, int ldx,
+                                  const float* __restrict__ w, int d, float eps, int8_t* __restrict__ xq, int ldq,
+                                  float* act_absmax, int32_t* row_sum, int32_t* status) {
+  extern __shared__ float row[];
+  __shared__ float bc;
+  __shared__ float red_f[32];
+  __shared__ int red_i[32];
+  int m = blockIdx.x;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float v = x[(size_t)m * ldx + i];
+    if (GATE_UP) {
+      float r = fmaxf(v, 0.0f);  // f32::max(0.0): NaN -> 0
+      v = __fmul_rn(__fmul_rn(r, r), x2[(size_t)m * ldx + i]);
+    }
+    row[i] = v;
+  }
+  __syncthreads();
+  float inv = rms_inv_exact(row, d, eps, &bc);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) row[i] = __fmul_rn(__fmul_rn(row[i], inv), w[i]);
+  __syncthreads();
+  quantize_row_smem(row, d, xq + (size_t)m * ldq, ldq, act_absmax + m, nullptr, row_sum + m, status, red_f, red_i);
+}
+
+void launch_norm_quant(const float* x, const float* x2, int ldx, const float* w, int d, float eps, int8_t* xq, int ldq,
+                       float* act_absmax, int32_t* row_sum, int32_t* status, int M, cudaStream_t st) {
+  if (M <= 0) return;
+  size_t smem = (size_t)d * sizeof(float);
+  if (x2)
+    norm_quant_kernel<true><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
+  else
+    norm_quant_kernel<false><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
+  count_launch();
+}
+
+// ---------------------------------------------------------------------------
+// Elementwise ops.
+// ---------------------------------------------------------------------------
+__global__ void squared_relu_kernel(float* x, size_t n) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    float r = fmaxf(x[i], 0.0f);
+    x[i] = __fmul_rn(r, r);
+  }
+}
+void launch_squared_relu(float* x, size_t n, cudaStream_t st) {
+  if (!n) return;
+  squared_relu_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(x, n);
+  count_launch();
+}
+
+__global__ void sqrelu_gate_kernel(const float* g, const float* u, float* o, size_t n) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    float r = fmaxf(g[i], 0.0f);
+    o[i] = __fmul_rn(__fmul_rn(r, r), u[i]);
+  }
+}
+void launch_sqrelu_gate(const float* g, const float* u, float* out, size_t n, cudaStream_t st) {
+  if (!n) return;
+  sqrelu_gate_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(g, u, out, n);
+  count_launch();
+}
+
+__global__ void elementwise_mul_kernel(const float* a, const float* b, float* o, size_t n) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) o[i] = __fmul_rn(a[i], b[i]);
+}
+void launch_elementwise_mul(const float* a, const float* b, float* out, size_t n, cudaStream_t st) {
+  if (!n) return;
+  elementwise_mul_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(a, b, out, n);
+  count_launch();
+}
+
+// expf of the reference (glibc) is evaluated here as exp in double rounded to
+// float: both are within one float ulp of the exact value and agree except
+// when the exact result is extremely close to a rounding boundary.
+__device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
+
+// softmax (activation.rs:230-255): max, exp(x - max), sequential sum, * 1/sum.
+__global__ void softmax_max_exp_kernel(float* x, size_t n, float* out_max) {
+  __shared__ float red[32];
+  float m = -INFINITY;
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = block_reduce(m, [](float a, float b) { return fmaxf(a, b); }, red);
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = exp_ref(__fsub_rn(x[i], m));
+  if (threadIdx.x == 0) *out_max = m;
+}
+__global__ void softmax_sum_kernel(const float* x, size_t n, float* out_inv) {
+  float s = 0.0f;
+  for (size_t i = 0; i < n; ++i) s = __fadd_rn(s, x[i]);
+  *out_inv = __fdiv_rn(1.0f, s);
+}
+__global__ void softmax_scale_kernel(float* x, size_t n, const float* inv) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = __fmul_rn(x[i], *inv);
+}
+void launch_softmax(float* x, size_t n, float* scratch, cudaStream_t st) {
+  if (!n) return;
+  softmax_max_exp_kernel<<<1, 1024, 0, st>>>(x, n, scratch);
+  softmax_sum_kernel<<<1, 1, 0, st>>>(x, n, scratch + 1);
+  softmax_scale_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(x, n, scratch + 1);
+  count_launch(3);
+}
+
+__global__ void embed_kernel(const uint16_t* __restrict__ embed, const uint32_t* __restrict__ tokens, int H,
+                             float* __restrict__ h, int32_t* status, int vocab) {
+  int t = blockIdx.x;
+  uint32_t tok = tokens[t];
+  if (tok >= (uint32_t)vocab) {
+    if (threadIdx.x == 0) atomicOr(status, 2);
+    tok = 0;
+  }
+  const uint16_t* row = embed + (size_t)tok * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) h[(size_t)t * H + i] = bf16_bits_to_f32(row[i]);
+}
+void launch_embed(const uint16_t* embed, const uint32_t* tokens, int T, int H, float* h, int32_t* status, int vocab,
+                  cudaStream_t st) {
+  if (T <= 0) return;
+  embed_kernel<<<T, 256, 0, st>>>(embed, tokens, H, h, status, vocab);
+  count_launch();
+}
+
+__global__ void gather_rows_kernel(const float* __restrict__ src, int ld, const int32_t* __restrict__ rows,
+                                   float* __restrict__ dst) {
+  const float* s = src + (size_t)rows[blockIdx.x] * ld;
+  for (int i = threadIdx.x; i < ld; i += blockDim.x) dst[(size_t)blockIdx.x * ld + i] = s[i];
+}
+void launch_gather_rows(const float* src, int ld, const int32_t* rows, int n, float* dst, cudaStream_t st) {
+  if (n <= 0) return;
+  gather_rows_kernel<<<n, 256, 0, st>>>(src, ld, rows, dst);
+  count_launch();
+}
+
+}  // namespace bitnet

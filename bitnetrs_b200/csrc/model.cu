@@ -1,0 +1,793 @@
+// model.cu — device-resident BitNet model, paged KV cache and the forward,
+// batched decode, ragged prefill and greedy generate entry points.
+//
+// Orchestration follows BitNetModel::forward / forward_into
+// (crates/bitnet-model/src/lib.rs:559-862, 931-1163) with the per-token GEMVs
+// batched into matmuls over all tokens of a step, the shared activation
+// quantisation fused into the preceding RMSNorm, the residual adds fused into
+// the o_proj / down_proj epilogues, and q/k/v (gate/up) projections fused into
+// one matmul each.  Every fused step computes the same f32 values as the
+// reference's separate calls.
+#include <algorithm>
+#include <tuple>
+#include <cmath>
+#include <cstring>
+
+#include "internal.h"
+
+using namespace bitnet;
+
+namespace {
+
+struct Layer {
+  uint32_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
+  float sq, sk, sv, so, sg, su, sd;
+  float *attn_norm = nullptr, *attn_sub_norm = nullptr, *ffn_norm = nullptr, *ffn_sub_norm = nullptr;
+};
+
+std::string sz(size_t v) { return std::to_string(v); }
+
+}  // namespace
+
+struct bitnet_cuda_model {
+  bitnet_cuda_ctx* ctx = nullptr;
+  bitnet_cuda_config cfg{};
+  int H = 0, hd = 0, nh = 0, nkv = 0, qd = 0, kvd = 0, F = 0, V = 0, L = 0, Tmax = 0;
+  int ldq = 0;  // row stride of the quantised activation buffer
+  std::vector<Layer> layers;
+  std::vector<void*> allocs;
+  uint16_t* embed = nullptr;
+  int8_t* lm_i8 = nullptr;
+  float* lm_scales = nullptr;
+  float* final_norm = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  // activations
+  float *h = nullptr, *qkv = nullptr, *qrot = nullptr, *attn = nullptr, *gu = nullptr, *hn = nullptr, *logits = nullptr;
+  int8_t* xq = nullptr;
+  float* amax = nullptr;
+  int32_t* rowsum = nullptr;
+  uint32_t *tokens = nullptr, *next = nullptr;
+  int32_t *tok_pos = nullptr, *tok_seq = nullptr, *last_row = nullptr, *status = nullptr;
+  DevBuf partial;
+  // pinned staging
+  int32_t* h_meta = nullptr;  // [2*Tmax + Tmax] pos, seq, last_row
+  uint32_t* h_tokens = nullptr;
+  // captured decode graphs, keyed by (kv, batch, timed), with their kernel
+  // counts and (when timed) the event pairs recorded around each launch
+  struct Graph {
+    cudaGraphExec_t exec;
+    uint64_t kernels;
+    std::vector<std::tuple<int, cudaEvent_t, cudaEvent_t>> marks;
+  };
+  std::map<std::tuple<void*, int, int>, Graph> graphs;
+  bool timing = false;
+  const Graph* last_timed = nullptr;
+  std::vector<std::tuple<int, cudaEvent_t, cudaEvent_t>>* marks = nullptr;  // set while capturing a timed graph
+
+  template <class T>
+  int alloc(T** p, size_t n) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<size_t>(n * sizeof(T), 16));
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc");
+    allocs.push_back(q);
+    *p = (T*)q;
+    return BITNET_OK;
+  }
+};
+
+struct bitnet_cuda_kv {
+  bitnet_cuda_model* model = nullptr;
+  KvGeom g;
+  int max_seqs = 0;
+  std::vector<int32_t> free_pages;
+  std::vector<std::vector<int32_t>> seq_pages;
+  std::vector<size_t> seq_len;
+  std::vector<int32_t> h_table;
+  int32_t* d_table = nullptr;
+  size_t capacity() const { return (size_t)g.max_pages_per_seq * kPage; }
+};
+
+namespace {
+
+// ModelConfig::validate (config.rs:110-150).
+int validate_config(const bitnet_cuda_config& c) {
+  if (c.hidden_size == 0) return config_error("hidden_size must be > 0");
+  if (c.num_attention_heads == 0) return config_error("num_attention_heads must be > 0");
+  if (c.num_key_value_heads == 0) return config_error("num_key_value_heads must be > 0");
+  if (c.hidden_size % c.num_attention_heads != 0)
+    return config_error("hidden_size (" + sz(c.hidden_size) + ") must be divisible by num_attention_heads (" +
+                        sz(c.num_attention_heads) + ")");
+  if (c.num_attention_heads % c.num_key_value_heads != 0)
+    return config_error("num_attention_heads (" + sz(c.num_attention_heads) +
+                        ") must be divisible by num_key_value_heads (" + sz(c.num_key_value_heads) + ")");
+  if (c.vocab_size == 0) return config_error("vocab_size must be > 0");
+  if (c.num_hidden_layers == 0) return config_error("num_hidden_layers must be > 0");
+  if (c.intermediate_size == 0) return config_error("intermediate_size must be > 0");
+  if (c.max_position_embeddings == 0) return config_error("max_position_embeddings must be > 0");
+  if (!(c.rope_theta > 0.0f)) return config_error("rope_theta must be > 0");
+  if (!(c.rms_norm_eps > 0.0f)) return config_error("rms_norm_eps must be > 0");
+  return BITNET_OK;
+}
+
+// Upload `rows` rows of a reference-format ternary tensor and repack them
+// into dst (device words) starting at row `row0`.
+int put_ternary(bitnet_cuda_model* m, const uint8_t* src, int rows, int cols, uint32_t* dst, int row0, DevBuf& tmp) {
+  if (!src) return shape_error("non-null ternary weight pointer", "null");
+  size_t pc = (size_t)(cols + 3) / 4;
+  BN_TRY(tmp.ensure((size_t)rows * pc));
+  BN_CUDA(cudaMemcpyAsync(tmp.p, src, (size_t)rows * pc, cudaMemcpyHostToDevice, m->ctx->stream));
+  launch_repack_ternary(tmp.as<uint8_t>(), dst + (size_t)row0 * words_per_row(cols), rows, cols, m->ctx->stream);
+  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));  // tmp is reused by the next tensor
+  return BITNET_OK;
+}
+
+template <class T>
+int put(bitnet_cuda_model* m, T** dst, const T* src, size_t n) {
+  if (!src) return shape_error("non-null weight pointer", "null");
+  BN_TRY(m->alloc(dst, n));
+  BN_CUDA(cudaMemcpyAsync(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice, m->ctx->stream));
+  return BITNET_OK;
+}
+
+int check_scale(float s, const char* what) {
+  if (!(s > 0.0f) || !std::isfinite(s)) return quant_error(std::string(what) + " scale must be finite and > 0");
+  return BITNET_OK;
+}
+
+// Ensure sequence `seq` has pages for positions [0, end); update the device table.
+int kv_reserve(bitnet_cuda_kv* kv, uint32_t seq, size_t end, cudaStream_t st) {
+  if (end > kv->capacity())
+    return shape_error("position < kv capacity (" + sz(kv->capacity()) + ")", "position = " + sz(end - 1));
+  auto& pages = kv->seq_pages[seq];
+  size_t need = (end + kPage - 1) / kPage;
+  if (need <= pages.size()) return BITNET_OK;
+  if (need - pages.size() > kv->free_pages.size()) return backend_error("paged KV cache is out of free pages");
+  size_t first = pages.size();
+  while (pages.size() < need) {
+    int32_t p = kv->free_pages.back();
+    kv->free_pages.pop_back();
+    kv->h_table[(size_t)seq * kv->g.max_pages_per_seq + pages.size()] = p;
+    pages.push_back(p);
+  }
+  int32_t* src = &kv->h_table[(size_t)seq * kv->g.max_pages_per_seq + first];
+  BN_CUDA(cudaMemcpyAsync(kv->d_table + (size_t)seq * kv->g.max_pages_per_seq + first, src,
+                          (need - first) * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  // the host table entries stay valid until the pages are freed; the copy
+  // must finish before they can change
+  BN_CUDA(cudaStreamSynchronize(st));
+  return BITNET_OK;
+}
+
+// Kernel classes for the per-step timing of device-resident decode graphs.
+enum KClass { kAttn = 0, kMatmul = 1, kNormQuant = 2, kRopeKv = 3, kLmHead = 4, kOther = 5, kClasses = 6 };
+
+// Records an event pair around `launch` when the graph being captured is timed.
+template <class F>
+void timed(bitnet_cuda_model* m, int cls, cudaStream_t st, F launch) {
+  if (!m->marks) {
+    launch();
+    return;
+  }
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, st);
+  launch();
+  cudaEventRecord(b, st);
+  m->marks->emplace_back(cls, a, b);
+}
+
+// Run the transformer over T tokens whose metadata (tokens, tok_pos, tok_seq,
+// last_row) is already on the device.  n_out rows of final hidden state
+// (selected by last_row) go through final norm, lm_head and argmax.
+void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int max_ctx, cudaStream_t st) {
+  const int H = m->H, qd = m->qd, kvd = m->kvd, F = m->F;
+  const float eps = m->cfg.rms_norm_eps;
+  const int nqkv = qd + 2 * kvd;
+  timed(m, kOther, st, [&] {
+    launch_embed(m->embed, m->tokens, T, H, m->h, m->status, m->V, st);
+  });
+  for (int l = 0; l < m->L; ++l) {
+    const Layer& Lw = m->layers[l];
+    // attention block
+    timed(m, kNormQuant, st, [&] {
+      launch_norm_quant(m->h, nullptr, H, Lw.attn_norm, H, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status, T, st);
+    });
+    Segments sqkv;
+    sqkv.n = 3;
+    sqkv.end[0] = qd;
+    sqkv.end[1] = qd + kvd;
+    sqkv.end[2] = nqkv;
+    sqkv.scale[0] = Lw.sq;
+    sqkv.scale[1] = Lw.sk;
+    sqkv.scale[2] = Lw.sv;
+    timed(m, kMatmul, st, [&] {
+      launch_ternary_matmul(Lw.wqkv, nqkv, H, m->xq, m->ldq, m->amax, m->rowsum, T, sqkv, Epi::Store, m->qkv, nqkv,
+                            nullptr, st);
+    });
+    timed(m, kRopeKv, st, [&] {
+      launch_rope_kv_store(m->qkv, nqkv, T, m->nh, m->nkv, m->hd, m->rope_cos, m->rope_sin, m->tok_pos, m->tok_seq,
+                           kv->d_table, kv->g, l, m->qrot, st);
+    });
+    timed(m, kAttn, st, [&] {
+      launch_paged_attention(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, m->attn,
+                             m->partial.as<float>(), m->partial.cap / 4, st);
+    });
+    timed(m, kNormQuant, st, [&] {
+      launch_norm_quant(m->attn, nullptr, qd, Lw.attn_sub_norm, qd, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status,
+                        T, st);
+    });
+    Segments so;
+    so.end[0] = so.end[1] = so.end[2] = H;
+    so.scale[0] = so.scale[1] = so.scale[2] = Lw.so;
+    timed(m, kMatmul, st, [&] {
+      launch_ternary_matmul(Lw.wo, H, qd, m->xq, m->ldq, m->amax, m->rowsum, T, so, Epi::Residual, m->h, H, nullptr, st);
+    });
+    // FFN block
+    timed(m, kNormQuant, st, [&] {
+      launch_norm_quant(m->h, nullptr, H, Lw.ffn_norm, H, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status, T, st);
+    });
+    Segments sgu;
+    sgu.n = 2;
+    sgu.end[0] = F;
+    sgu.end[1] = sgu.end[2] = 2 * F;
+    sgu.scale[0] = Lw.sg;
+    sgu.scale[1] = sgu.scale[2] = Lw.su;
+    timed(m, kMatmul, st, [&] {
+      launch_ternary_matmul(Lw.wgu, 2 * F, H, m->xq, m->ldq, m->amax, m->rowsum, T, sgu, Epi::Store, m->gu, 2 * F,
+                            nullptr, st);
+    });
+    timed(m, kNormQuant, st, [&] {
+      launch_norm_quant(m->gu, m->gu + F, 2 * F, Lw.ffn_sub_norm, F, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status,
+                        T, st);
+    });
+    Segments sd;
+    sd.end[0] = sd.end[1] = sd.end[2] = H;
+    sd.scale[0] = sd.scale[1] = sd.scale[2] = Lw.sd;
+    timed(m, kMatmul, st, [&] {
+      launch_ternary_matmul(Lw.wdown, H, F, m->xq, m->ldq, m->amax, m->rowsum, T, sd, Epi::Residual, m->h, H, nullptr,
+                            st);
+    });
+  }
+  // final norm on the selected rows, lm_head, greedy argmax
+  timed(m, kOther, st, [&] {
+    launch_gather_rows(m->h, H, m->last_row, n_out, m->qrot, st);
+  });
+  timed(m, kOther, st, [&] {
+    launch_rms_norm(m->qrot, H, m->final_norm, H, eps, m->hn, H, n_out, st);
+  });
+  timed(m, kLmHead, st, [&] {
+    launch_lm_head(m->lm_i8, LmW::I8, m->lm_scales, m->hn, H, n_out, m->V, H, m->logits, m->V, st);
+  });
+  timed(m, kOther, st, [&] {
+    launch_argmax(m->logits, m->V, n_out, m->V, m->next, st);
+  });
+}
+
+int check_status(bitnet_cuda_model* m) {
+  int32_t s = 0;
+  BN_CUDA(cudaMemcpyAsync(&s, m->status, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (s & 2) return shape_error("token id < vocab_size", "out-of-range token id");
+  if (s & 1) return quant_error("non-finite activation value in the forward pass");
+  return BITNET_OK;
+}
+
+// Host-side bookkeeping for a batch of (seq, n_tokens) appended at each
+// sequence's current length: reserve pages, fill the pinned metadata.
+int prepare_batch(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t n_seqs, const uint32_t* seq_ids,
+                  const uint32_t* counts, int* T_out, int* max_ctx_out, cudaStream_t st) {
+  size_t T = 0;
+  for (size_t i = 0; i < n_seqs; ++i) {
+    if (seq_ids[i] >= (uint32_t)kv->max_seqs)
+      return shape_error("seq id < max_seqs (" + sz(kv->max_seqs) + ")", "seq id " + sz(seq_ids[i]));
+    for (size_t j = 0; j < i; ++j)
+      if (seq_ids[j] == seq_ids[i]) return shape_error("distinct sequence ids in one batch", "duplicate " + sz(seq_ids[i]));
+    if (counts[i] == 0) return shape_error("tokens.len() > 0", "0 tokens for a sequence");
+    T += counts[i];
+  }
+  if (T > (size_t)m->Tmax) return shape_error("batch tokens <= " + sz(m->Tmax), sz(T));
+  int max_ctx = 1;
+  size_t t = 0;
+  for (size_t i = 0; i < n_seqs; ++i) {
+    uint32_t s = seq_ids[i];
+    size_t start = kv->seq_len[s], end = start + counts[i];
+    if (end > m->cfg.max_position_embeddings)
+      return shape_error("sequence position <= max_position_embeddings " + sz(m->cfg.max_position_embeddings),
+                         "position " + sz(end));
+    BN_TRY(kv_reserve(kv, s, end, st));
+    for (size_t j = 0; j < counts[i]; ++j, ++t) {
+      m->h_meta[t] = (int32_t)(start + j);
+      m->h_meta[m->Tmax + t] = (int32_t)s;
+    }
+    m->h_meta[2 * m->Tmax + i] = (int32_t)(t - 1);
+    max_ctx = std::max<int>(max_ctx, (int)end);
+  }
+  *T_out = (int)T;
+  *max_ctx_out = max_ctx;
+  return BITNET_OK;
+}
+
+int upload_meta(bitnet_cuda_model* m, int T, int n_out, cudaStream_t st) {
+  BN_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_meta, T * 4, cudaMemcpyHostToDevice, st));
+  BN_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_meta + m->Tmax, T * 4, cudaMemcpyHostToDevice, st));
+  BN_CUDA(cudaMemcpyAsync(m->last_row, m->h_meta + 2 * m->Tmax, n_out * 4, cudaMemcpyHostToDevice, st));
+  return BITNET_OK;
+}
+
+void destroy_graph(bitnet_cuda_model::Graph& g) {
+  cudaGraphExecDestroy(g.exec);
+  for (auto& t : g.marks) {
+    cudaEventDestroy(std::get<1>(t));
+    cudaEventDestroy(std::get<2>(t));
+  }
+}
+
+void drop_graphs(bitnet_cuda_model* m) {
+  for (auto& kvp : m->graphs) destroy_graph(kvp.second);
+  m->graphs.clear();
+  m->last_timed = nullptr;
+}
+
+int ensure_partial(bitnet_cuda_model* m, int T, int max_ctx) {
+  size_t bytes = paged_attention_partial_floats(T, m->nh, m->hd, max_ctx) * sizeof(float);
+  if (bytes <= m->partial.cap) return BITNET_OK;
+  // captured graphs hold the old address
+  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  drop_graphs(m);
+  return m->partial.ensure(bytes);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const bitnet_cuda_weights* w,
+                             uint32_t max_batch_tokens, bitnet_cuda_model** out) {
+  if (!out || !cfg || !w || !ctx) return shape_error("non-null arguments", "null");
+  *out = nullptr;
+  BN_TRY(validate_config(*cfg));
+  if (max_batch_tokens == 0) return shape_error("max_batch_tokens > 0", "0");
+  if (!w->layers) return shape_error("non-null layers", "null");
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  cudaSetDevice(ctx->device);
+  auto* m = new bitnet_cuda_model();
+  m->ctx = ctx;
+  m->cfg = *cfg;
+  m->H = (int)cfg->hidden_size;
+  m->nh = (int)cfg->num_attention_heads;
+  m->nkv = (int)cfg->num_key_value_heads;
+  m->hd = m->H / m->nh;
+  m->qd = m->nh * m->hd;
+  m->kvd = m->nkv * m->hd;
+  m->F = (int)cfg->intermediate_size;
+  m->V = (int)cfg->vocab_size;
+  m->L = (int)cfg->num_hidden_layers;
+  m->Tmax = (int)max_batch_tokens;
+  m->ldq = (int)std::max({padded_cols(m->H), padded_cols(m->qd), padded_cols(m->F)});
+  auto fail = [&](int rc) {
+    bitnet_cuda_model_destroy(m);
+    return rc;
+  };
+  int rc;
+  DevBuf tmp;
+  const int H = m->H, qd = m->qd, kvd = m->kvd, F = m->F;
+  for (int l = 0; l < m->L; ++l) {
+    const bitnet_cuda_layer_weights& s = w->layers[l];
+    Layer Lw;
+    Lw.sq = s.q_scale;
+    Lw.sk = s.k_scale;
+    Lw.sv = s.v_scale;
+    Lw.so = s.o_scale;
+    Lw.sg = s.gate_scale;
+    Lw.su = s.up_scale;
+    Lw.sd = s.down_scale;
+    for (float sc : {s.q_scale, s.k_scale, s.v_scale, s.o_scale, s.gate_scale, s.up_scale, s.down_scale})
+      if ((rc = check_scale(sc, "projection"))) return fail(rc);
+    if ((rc = m->alloc(&Lw.wqkv, (size_t)(qd + 2 * kvd) * words_per_row(H)))) return fail(rc);
+    if ((rc = m->alloc(&Lw.wo, (size_t)H * words_per_row(qd)))) return fail(rc);
+    if ((rc = m->alloc(&Lw.wgu, (size_t)2 * F * words_per_row(H)))) return fail(rc);
+    if ((rc = m->alloc(&Lw.wdown, (size_t)H * words_per_row(F)))) return fail(rc);
+    if ((rc = put_ternary(m, s.q_proj, qd, H, Lw.wqkv, 0, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, s.k_proj, kvd, H, Lw.wqkv, qd, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, s.v_proj, kvd, H, Lw.wqkv, qd + kvd, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, s.o_proj, H, qd, Lw.wo, 0, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, s.gate_proj, F, H, Lw.wgu, 0, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, s.up_proj, F, H, Lw.wgu, F, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, s.down_proj, H, F, Lw.wdown, 0, tmp))) return fail(rc);
+    if ((rc = put(m, &Lw.attn_norm, s.attention_norm, H))) return fail(rc);
+    if ((rc = put(m, &Lw.attn_sub_norm, s.attn_sub_norm, qd))) return fail(rc);
+    if ((rc = put(m, &Lw.ffn_norm, s.ffn_norm, H))) return fail(rc);
+    if ((rc = put(m, &Lw.ffn_sub_norm, s.ffn_sub_norm, F))) return fail(rc);
+    m->layers.push_back(Lw);
+  }
+  const size_t V = m->V;
+  if ((rc = put(m, &m->embed, w->embed_tokens, V * H))) return fail(rc);
+  if ((rc = put(m, &m->lm_i8, w->lm_head_i8, V * H))) return fail(rc);
+  if ((rc = put(m, &m->lm_scales, w->lm_head_scales, V))) return fail(rc);
+  if ((rc = put(m, &m->final_norm, w->final_norm, H))) return fail(rc);
+  // RoPE table for every position the model accepts (rope.rs:100-147).
+  std::vector<float> cs, sn;
+  if ((rc = build_rope_host(cfg->max_position_embeddings, m->hd, cfg->rope_theta, cs, sn))) return fail(rc);
+  if ((rc = put(m, &m->rope_cos, cs.data(), cs.size()))) return fail(rc);
+  if ((rc = put(m, &m->rope_sin, sn.data(), sn.size()))) return fail(rc);
+  // activations
+  const size_t T = m->Tmax;
+  const size_t R = std::min<size_t>(T, 1024);  // logits rows per forward
+  if ((rc = m->alloc(&m->h, T * H))) return fail(rc);
+  if ((rc = m->alloc(&m->qkv, T * (qd + 2 * kvd)))) return fail(rc);
+  if ((rc = m->alloc(&m->qrot, T * std::max(qd, H)))) return fail(rc);
+  if ((rc = m->alloc(&m->attn, T * qd))) return fail(rc);
+  if ((rc = m->alloc(&m->gu, T * 2 * F))) return fail(rc);
+  if ((rc = m->alloc(&m->hn, R * H))) return fail(rc);
+  if ((rc = m->alloc(&m->logits, R * V))) return fail(rc);
+  if ((rc = m->alloc(&m->xq, T * m->ldq))) return fail(rc);
+  if ((rc = m->alloc(&m->amax, T))) return fail(rc);
+  if ((rc = m->alloc(&m->rowsum, T))) return fail(rc);
+  if ((rc = m->alloc(&m->tokens, T))) return fail(rc);
+  if ((rc = m->alloc(&m->next, T))) return fail(rc);
+  if ((rc = m->alloc(&m->tok_pos, T))) return fail(rc);
+  if ((rc = m->alloc(&m->tok_seq, T))) return fail(rc);
+  if ((rc = m->alloc(&m->last_row, T))) return fail(rc);
+  if ((rc = m->alloc(&m->status, 16))) return fail(rc);
+  cudaError_t e = cudaMallocHost(&m->h_meta, 3 * T * sizeof(int32_t));
+  if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
+  e = cudaMallocHost(&m->h_tokens, T * sizeof(uint32_t));
+  if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
+  e = cudaMemsetAsync(m->status, 0, 64, ctx->stream);
+  if (e != cudaSuccess) return fail(cuda_error(e, "cudaMemset"));
+  e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return fail(cuda_error(e, "model upload"));
+  *out = m;
+  return BITNET_OK;
+}
+
+void bitnet_cuda_model_destroy(bitnet_cuda_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  drop_graphs(m);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->h_meta) cudaFreeHost(m->h_meta);
+  if (m->h_tokens) cudaFreeHost(m->h_tokens);
+  m->partial.release();
+  delete m;
+}
+
+// ---- KV cache -----------------------------------------------------------------
+int bitnet_cuda_kv_create(bitnet_cuda_model* m, uint32_t num_pages, uint32_t max_seqs, int kv_dtype,
+                          bitnet_cuda_kv** out) {
+  if (!out || !m) return shape_error("non-null arguments", "null");
+  *out = nullptr;
+  if (num_pages == 0 || max_seqs == 0) return shape_error("num_pages > 0 and max_seqs > 0", "0");
+  if (kv_dtype != BITNET_KV_F32 && kv_dtype != BITNET_KV_BF16) return config_error("kv_dtype must be F32 or BF16");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  auto* kv = new bitnet_cuda_kv();
+  kv->model = m;
+  kv->g.bf16 = kv_dtype == BITNET_KV_BF16;
+  kv->g.pages = (int)num_pages;
+  kv->g.kv_heads = m->nkv;
+  kv->g.hd = m->hd;
+  kv->g.layers = m->L;
+  kv->g.max_pages_per_seq = (int)ceil_div(m->cfg.max_position_embeddings, kPage);
+  kv->max_seqs = (int)max_seqs;
+  size_t elem = kv->g.bf16 ? 2 : 4;
+  size_t bytes = (size_t)m->L * num_pages * m->nkv * 2 * kPage * m->hd * elem;
+  cudaError_t e = cudaMalloc(&kv->g.pool, bytes);
+  if (e != cudaSuccess) {
+    delete kv;
+    return cuda_error(e, "cudaMalloc(kv pool)");
+  }
+  size_t tbl = (size_t)max_seqs * kv->g.max_pages_per_seq;
+  e = cudaMalloc(&kv->d_table, tbl * sizeof(int32_t));
+  if (e != cudaSuccess) {
+    cudaFree(kv->g.pool);
+    delete kv;
+    return cuda_error(e, "cudaMalloc(page table)");
+  }
+  cudaMemsetAsync(kv->d_table, 0, tbl * sizeof(int32_t), m->ctx->stream);
+  cudaStreamSynchronize(m->ctx->stream);
+  kv->h_table.assign(tbl, 0);
+  kv->free_pages.resize(num_pages);
+  for (uint32_t i = 0; i < num_pages; ++i) kv->free_pages[i] = (int32_t)(num_pages - 1 - i);
+  kv->seq_pages.assign(max_seqs, {});
+  kv->seq_len.assign(max_seqs, 0);
+  *out = kv;
+  return BITNET_OK;
+}
+
+void bitnet_cuda_kv_destroy(bitnet_cuda_kv* kv) {
+  if (!kv) return;
+  bitnet_cuda_model* m = kv->model;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (auto it = m->graphs.begin(); it != m->graphs.end();) {
+    if (std::get<0>(it->first) == (void*)kv) {
+      if (m->last_timed == &it->second) m->last_timed = nullptr;
+      destroy_graph(it->second);
+      it = m->graphs.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  cudaFree(kv->g.pool);
+  cudaFree(kv->d_table);
+  delete kv;
+}
+
+int bitnet_cuda_kv_seq_reset(bitnet_cuda_kv* kv, uint32_t seq) {
+  if (seq >= (uint32_t)kv->max_seqs) return shape_error("seq < max_seqs", sz(seq));
+  for (int32_t p : kv->seq_pages[seq]) kv->free_pages.push_back(p);
+  kv->seq_pages[seq].clear();
+  kv->seq_len[seq] = 0;
+  return BITNET_OK;
+}
+
+int bitnet_cuda_kv_seq_len(bitnet_cuda_kv* kv, uint32_t seq, size_t* len) {
+  if (seq >= (uint32_t)kv->max_seqs) return shape_error("seq < max_seqs", sz(seq));
+  *len = kv->seq_len[seq];
+  return BITNET_OK;
+}
+
+int bitnet_cuda_kv_free_pages(bitnet_cuda_kv* kv, size_t* n) {
+  *n = kv->free_pages.size();
+  return BITNET_OK;
+}
+
+int bitnet_cuda_kv_seq_reserve(bitnet_cuda_kv* kv, uint32_t seq, size_t len) {
+  if (seq >= (uint32_t)kv->max_seqs) return shape_error("seq < max_seqs", sz(seq));
+  std::lock_guard<std::mutex> lk(kv->model->ctx->mu);
+  cudaSetDevice(kv->model->ctx->device);
+  return kv_reserve(kv, seq, len, kv->model->ctx->stream);
+}
+
+static int kv_seq_copy(bitnet_cuda_kv* kv, uint32_t seq, size_t n, const float* k, float* kout, const float* v,
+                       float* vout, bool to_cache) {
+  if (seq >= (uint32_t)kv->max_seqs) return shape_error("seq < max_seqs", sz(seq));
+  bitnet_cuda_model* m = kv->model;
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t st = m->ctx->stream;
+  if (!to_cache && n > kv->seq_len[seq]) return shape_error("n <= sequence length " + sz(kv->seq_len[seq]), sz(n));
+  if (to_cache) BN_TRY(kv_reserve(kv, seq, n, st));
+  if (n == 0) {
+    if (to_cache) kv->seq_len[seq] = 0;
+    return BITNET_OK;
+  }
+  size_t elems = (size_t)m->L * n * m->kvd;
+  DevBuf ks, vs;
+  BN_TRY(ks.ensure(elems * 4));
+  BN_TRY(vs.ensure(elems * 4));
+  const int32_t* row = kv->d_table + (size_t)seq * kv->g.max_pages_per_seq;
+  if (to_cache) {
+    BN_CUDA(cudaMemcpyAsync(ks.p, k, elems * 4, cudaMemcpyHostToDevice, st));
+    BN_CUDA(cudaMemcpyAsync(vs.p, v, elems * 4, cudaMemcpyHostToDevice, st));
+    launch_kv_copy(kv->g, row, (int)n, ks.as<float>(), vs.as<float>(), true, st);
+    kv->seq_len[seq] = n;
+  } else {
+    launch_kv_copy(kv->g, row, (int)n, ks.as<float>(), vs.as<float>(), false, st);
+    BN_CUDA(cudaMemcpyAsync(kout, ks.p, elems * 4, cudaMemcpyDeviceToHost, st));
+    BN_CUDA(cudaMemcpyAsync(vout, vs.p, elems * 4, cudaMemcpyDeviceToHost, st));
+  }
+  BN_CUDA(cudaGetLastError());
+  BN_CUDA(cudaStreamSynchronize(st));
+  return BITNET_OK;
+}
+
+int bitnet_cuda_kv_seq_write(bitnet_cuda_kv* kv, uint32_t seq, size_t n, const float* k, const float* v) {
+  return kv_seq_copy(kv, seq, n, k, nullptr, v, nullptr, true);
+}
+
+int bitnet_cuda_kv_seq_read(bitnet_cuda_kv* kv, uint32_t seq, size_t n, float* k, float* v) {
+  return kv_seq_copy(kv, seq, n, nullptr, k, nullptr, v, false);
+}
+
+int bitnet_cuda_kv_seq_fill_random(bitnet_cuda_kv* kv, uint32_t seq, size_t n, uint64_t seed) {
+  if (seq >= (uint32_t)kv->max_seqs) return shape_error("seq < max_seqs", sz(seq));
+  bitnet_cuda_model* m = kv->model;
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t st = m->ctx->stream;
+  BN_TRY(kv_reserve(kv, seq, n, st));
+  launch_kv_fill_random(kv->g, kv->d_table + (size_t)seq * kv->g.max_pages_per_seq, (int)n, seed, seq, st);
+  BN_CUDA(cudaGetLastError());
+  BN_CUDA(cudaStreamSynchronize(st));
+  kv->seq_len[seq] = n;
+  return BITNET_OK;
+}
+
+// ---- forward / decode / prefill ------------------------------------------------------
+static int forward_common(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t n_seqs, const uint32_t* seq_ids,
+                          const uint32_t* counts, const uint32_t* tokens, float* logits, uint32_t* next) {
+  cudaStream_t st = m->ctx->stream;
+  int T = 0, max_ctx = 1;
+  BN_TRY(prepare_batch(m, kv, n_seqs, seq_ids, counts, &T, &max_ctx, st));
+  if (n_seqs > 1024) return shape_error("<= 1024 sequences per call", sz(n_seqs));
+  BN_TRY(ensure_partial(m, T, max_ctx));
+  std::memcpy(m->h_tokens, tokens, (size_t)T * 4);
+  BN_CUDA(cudaMemcpyAsync(m->tokens, m->h_tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  BN_TRY(upload_meta(m, T, (int)n_seqs, st));
+  run_forward(m, kv, T, (int)n_seqs, max_ctx, st);
+  BN_CUDA(cudaGetLastError());
+  if (logits) BN_CUDA(cudaMemcpyAsync(logits, m->logits, n_seqs * m->V * 4, cudaMemcpyDeviceToHost, st));
+  if (next) BN_CUDA(cudaMemcpyAsync(next, m->next, n_seqs * 4, cudaMemcpyDeviceToHost, st));
+  BN_TRY(check_status(m));
+  for (size_t i = 0; i < n_seqs; ++i) kv->seq_len[seq_ids[i]] += counts[i];
+  return BITNET_OK;
+}
+
+int bitnet_cuda_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* tokens, size_t n,
+                        size_t start_pos, float* logits) {
+  if (!m || !kv) return shape_error("non-null model and kv", "null");
+  if (n == 0) return shape_error("tokens must not be empty", "0 tokens");
+  if (seq >= (uint32_t)kv->max_seqs) return shape_error("seq < max_seqs", sz(seq));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  size_t len = kv->seq_len[seq];
+  if (start_pos > len) return shape_error("start_pos <= cached positions (" + sz(len) + ")", "start_pos = " + sz(start_pos));
+  kv->seq_len[seq] = start_pos;  // positions >= start_pos are overwritten
+  // chunk long inputs by the model's token capacity (same per-token math)
+  size_t done = 0;
+  while (done < n) {
+    uint32_t cnt = (uint32_t)std::min<size_t>(n - done, (size_t)m->Tmax);
+    bool last = done + cnt == n;
+    BN_TRY(forward_common(m, kv, 1, &seq, &cnt, tokens + done, last ? logits : nullptr, nullptr));
+    done += cnt;
+  }
+  return BITNET_OK;
+}
+
+int bitnet_cuda_prefill(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t n_seqs, const uint32_t* seq_ids,
+                        const uint32_t* tokens, const uint32_t* cu_seqlens, float* logits, uint32_t* next_tokens) {
+  if (!m || !kv) return shape_error("non-null model and kv", "null");
+  if (n_seqs == 0) return BITNET_OK;
+  std::vector<uint32_t> counts(n_seqs);
+  for (size_t i = 0; i < n_seqs; ++i) {
+    if (cu_seqlens[i + 1] < cu_seqlens[i]) return shape_error("non-decreasing cu_seqlens", "decreasing");
+    counts[i] = cu_seqlens[i + 1] - cu_seqlens[i];
+  }
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  return forward_common(m, kv, n_seqs, seq_ids, counts.data(), tokens + cu_seqlens[0], logits, next_tokens);
+}
+
+// One decode step as a CUDA graph: tokens come from `src` (host or device),
+// next tokens / logits stay in the model's device buffers.
+static int decode_graph(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t batch, const uint32_t* seq_ids,
+                        const uint32_t* src, bool src_on_host, cudaStream_t st) {
+  if (batch > 1024) return shape_error("batch <= 1024", sz(batch));
+  std::vector<uint32_t> ones(batch, 1);
+  int T = 0, max_ctx = 1;
+  BN_TRY(prepare_batch(m, kv, batch, seq_ids, ones.data(), &T, &max_ctx, st));
+  // The graph is sized for the cache capacity so it can be replayed as
+  // contexts grow; splits past a token's context exit immediately.
+  const int cap_ctx = (int)kv->capacity();
+  BN_TRY(ensure_partial(m, T, cap_ctx));
+  BN_TRY(upload_meta(m, T, T, st));
+  if (src_on_host) {
+    std::memcpy(m->h_tokens, src, (size_t)T * 4);
+    BN_CUDA(cudaMemcpyAsync(m->tokens, m->h_tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  } else {
+    BN_CUDA(cudaMemcpyAsync(m->tokens, src, (size_t)T * 4, cudaMemcpyDeviceToDevice, st));
+  }
+  auto key = std::make_tuple((void*)kv, T, m->timing ? 1 : 0);
+  auto it = m->graphs.find(key);
+  if (it == m->graphs.end()) {
+    bitnet_cuda_model::Graph gr{};
+    cudaGraph_t g;
+    uint64_t before = launches_total();
+    if (m->timing) m->marks = &gr.marks;
+    cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      run_forward(m, kv, T, T, cap_ctx, st);
+      e = cudaStreamEndCapture(st, &g);
+    }
+    m->marks = nullptr;
+    gr.kernels = launches_total() - before;
+    uncount_launch(gr.kernels);  // captured, not launched: replays count them
+    if (e != cudaSuccess) {
+      destroy_graph(gr);
+      return cuda_error(e, "CUDA graph capture");
+    }
+    e = cudaGraphInstantiate(&gr.exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGraphInstantiate");
+    it = m->graphs.emplace(key, std::move(gr)).first;
+  }
+  BN_CUDA(cudaGraphLaunch(it->second.exec, st));
+  count_launch(it->second.kernels);
+  if (m->timing) m->last_timed = &it->second;
+  for (size_t i = 0; i < batch; ++i) kv->seq_len[seq_ids[i]] += 1;
+  return BITNET_OK;
+}
+
+int bitnet_cuda_decode_step(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t batch, const uint32_t* seq_ids,
+                            const uint32_t* tokens, float* logits, uint32_t* next_tokens) {
+  if (!m || !kv) return shape_error("non-null model and kv", "null");
+  if (batch == 0) return BITNET_OK;
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t st = m->ctx->stream;
+  BN_TRY(decode_graph(m, kv, batch, seq_ids, tokens, true, st));
+  if (logits) BN_CUDA(cudaMemcpyAsync(logits, m->logits, batch * m->V * 4, cudaMemcpyDeviceToHost, st));
+  if (next_tokens) BN_CUDA(cudaMemcpyAsync(next_tokens, m->next, batch * 4, cudaMemcpyDeviceToHost, st));
+  return check_status(m);  // synchronises
+}
+
+int bitnet_cuda_decode_step_device(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t batch, const uint32_t* seq_ids,
+                                   const uint32_t* d_tokens, uint32_t* d_next, float* d_logits, void* stream) {
+  if (!m || !kv) return shape_error("non-null model and kv", "null");
+  if (batch == 0) return BITNET_OK;
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : m->ctx->stream;
+  BN_TRY(decode_graph(m, kv, batch, seq_ids, d_tokens, false, st));
+  BN_CUDA(cudaMemcpyAsync(d_next, m->next, batch * 4, cudaMemcpyDeviceToDevice, st));
+  if (d_logits) BN_CUDA(cudaMemcpyAsync(d_logits, m->logits, batch * m->V * 4, cudaMemcpyDeviceToDevice, st));
+  return BITNET_OK;
+}
+
+int bitnet_cuda_model_set_kernel_timing(bitnet_cuda_model* m, int enable) {
+  if (!m) return shape_error("non-null model", "null");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  m->timing = enable != 0;
+  return BITNET_OK;
+}
+
+int bitnet_cuda_model_kernel_times(bitnet_cuda_model* m, float* ms, int32_t* launches) {
+  if (!m || !ms || !launches) return shape_error("non-null arguments", "null");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  for (int c = 0; c < kClasses; ++c) {
+    ms[c] = 0.0f;
+    launches[c] = 0;
+  }
+  if (!m->last_timed) return backend_error("no timed decode step has run");
+  for (const auto& t : m->last_timed->marks) {
+    BN_CUDA(cudaEventSynchronize(std::get<2>(t)));
+    float e = 0.0f;
+    BN_CUDA(cudaEventElapsedTime(&e, std::get<1>(t), std::get<2>(t)));
+    ms[std::get<0>(t)] += e;
+    launches[std::get<0>(t)] += 1;
+  }
+  return BITNET_OK;
+}
+
+int bitnet_cuda_model_check(bitnet_cuda_model* m) {
+  if (!m) return shape_error("non-null model", "null");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  int rc = check_status(m);
+  BN_CUDA(cudaMemsetAsync(m->status, 0, 64, m->ctx->stream));
+  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  return rc;
+}
+
+int bitnet_cuda_generate(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* prompt,
+                         size_t n_prompt, size_t max_new, uint32_t eos0, uint32_t eos1, uint32_t* out_tokens,
+                         size_t* n_out) {
+  if (!n_out) return shape_error("non-null n_out", "null");
+  *n_out = 0;
+  if (n_prompt == 0) return BITNET_OK;
+  BN_TRY(bitnet_cuda_kv_seq_reset(kv, seq));
+  uint32_t next = 0;
+  {
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaSetDevice(m->ctx->device);
+    size_t done = 0;
+    while (done < n_prompt) {
+      uint32_t cnt = (uint32_t)std::min<size_t>(n_prompt - done, (size_t)m->Tmax);
+      BN_TRY(forward_common(m, kv, 1, &seq, &cnt, prompt + done, nullptr, &next));
+      done += cnt;
+    }
+  }
+  for (size_t step = 0; step < max_new; ++step) {
+    if (next == eos0 || next == eos1) break;
+    out_tokens[(*n_out)++] = next;
+    BN_TRY(bitnet_cuda_decode_step(m, kv, 1, &seq, &next, nullptr, &next));
+  }
+  return BITNET_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,310 @@
+/*
+ * bitnet_cuda.h — C ABI of the B200 (sm_100a) backend for bitnetrs.
+ *
+ * The library is a drop-in for the reference's operator boundary, the Rust
+ * trait `bitnet_core::backend::Backend` (crates/bitnet-core/src/backend/mod.rs:128-517),
+ * selected by `Device::Gpu { device_id }` in `create_backend`
+ * (crates/bitnet-model/src/device.rs:79-121).  Every trait method has one
+ * entry point below taking plain host pointers plus the length of every
+ * slice, so the Rust shim can forward `&[T]` / `&mut [T]` without copies and
+ * the library can reproduce the reference's shape validation.
+ *
+ * Beyond the trait, the library keeps weights and a paged KV cache resident
+ * in HBM and exposes whole-forward entry points (BitNetModel::forward_into,
+ * batched decode / prefill, greedy generate) — the reference's per-op host
+ * slices cannot reach the device roofline.
+ *
+ * Conventions
+ *  - Return value: BITNET_OK or one of the error codes, mirroring the
+ *    BitNetError variants (crates/bitnet-core/src/error.rs:12-60).  The
+ *    message of the last failure on the calling thread is returned by
+ *    bitnet_cuda_last_error().  No entry point aborts the process and none
+ *    falls back to the CPU.
+ *  - Host pointers are only read/written during the call.  Outputs are
+ *    caller-allocated and overwritten.
+ *  - Entry points suffixed _device take device pointers and a cudaStream_t
+ *    (passed as void*; NULL selects the context's stream) and return without
+ *    synchronising.
+ *  - A context is bound to one GPU.  Calls on one context are serialised by
+ *    an internal mutex, so the handle is Send + Sync like the trait requires.
+ */
+#ifndef BITNET_CUDA_H
+#define BITNET_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- error codes (BitNetError, crates/bitnet-core/src/error.rs:12-60) ---- */
+#define BITNET_OK 0
+#define BITNET_ERR_INVALID_SHAPE 1  /* BitNetError::InvalidShape { expected, got } */
+#define BITNET_ERR_QUANTIZATION 2   /* BitNetError::QuantizationError(msg)          */
+#define BITNET_ERR_BACKEND 3        /* BitNetError::BackendError { "CUDA", msg }     */
+#define BITNET_ERR_INVALID_CONFIG 4 /* BitNetError::InvalidConfig(msg)              */
+
+typedef struct bitnet_cuda_ctx bitnet_cuda_ctx;
+typedef struct bitnet_cuda_model bitnet_cuda_model;
+typedef struct bitnet_cuda_kv bitnet_cuda_kv;
+typedef struct bitnet_cuda_weight bitnet_cuda_weight;
+
+/* ===================================================================== */
+/* Lifecycle                                                              */
+/* ===================================================================== */
+
+/* Replaces CudaBackend::new (crates/bitnet-gpu-cuda/src/lib.rs:94-104), which
+ * is a stub in the reference; device_id is the CUDA ordinal. */
+int bitnet_cuda_create(uint32_t device_id, bitnet_cuda_ctx** out);
+void bitnet_cuda_destroy(bitnet_cuda_ctx* ctx);
+
+/* Backend::device_name (mod.rs:516). */
+const char* bitnet_cuda_device_name(const bitnet_cuda_ctx* ctx);
+
+/* Message of the last failing call made by this thread ("" if none). */
+const char* bitnet_cuda_last_error(void);
+
+/* Library version string. */
+const char* bitnet_cuda_version(void);
+
+/* ===================================================================== */
+/* Backend trait methods (host slices)                                    */
+/* ===================================================================== */
+
+/* Backend::ternary_gemv (mod.rs:152-160); CpuBackend: gemv.rs:108-165.
+ * out[i] = ws * sum_j W[i,j] * x[j], f32 accumulation in the reference's order. */
+int bitnet_cuda_ternary_gemv(bitnet_cuda_ctx* ctx, const uint8_t* weight_packed, size_t weight_len,
+                             float weight_scale, const float* input, size_t input_len, float* output,
+                             size_t output_len, size_t out_features, size_t in_features);
+
+/* Backend::ternary_gemv_with_activation_quant (mod.rs:185-207); CpuBackend
+ * override cpu/src/lib.rs:223-249 (absmax int8 quantisation + int32 GEMV). */
+int bitnet_cuda_ternary_gemv_with_activation_quant(bitnet_cuda_ctx* ctx, const uint8_t* weight_packed,
+                                                   size_t weight_len, float weight_scale, const float* input,
+                                                   size_t input_len, float* output, size_t output_len,
+                                                   size_t out_features, size_t in_features);
+
+/* Backend::rms_norm (mod.rs:225); cpu/src/norm.rs:77-137. */
+int bitnet_cuda_rms_norm(bitnet_cuda_ctx* ctx, const float* input, size_t input_len, const float* weight,
+                         size_t weight_len, float eps, float* output, size_t output_len);
+
+/* Backend::rope_embed (mod.rs:251-260); cpu/src/lib.rs:289-314 + rope.rs:312-355.
+ * q and k are rotated in place (half-split convention). */
+int bitnet_cuda_rope_embed(bitnet_cuda_ctx* ctx, float* q, size_t q_len, float* k, size_t k_len, size_t position,
+                           size_t head_dim, size_t n_heads, size_t n_kv_heads, float theta);
+
+/* Backend::masked_attention (mod.rs:301-311); cpu/src/attention.rs:97-209.
+ * k_cache / v_cache are head-major [n_kv_heads][max_seq][head_dim]. */
+int bitnet_cuda_masked_attention(bitnet_cuda_ctx* ctx, const float* q, size_t q_len, const float* k_cache,
+                                 size_t k_len, const float* v_cache, size_t v_len, float* output, size_t output_len,
+                                 size_t n_heads, size_t n_kv_heads, size_t head_dim, size_t cur_pos);
+
+/* Backend::squared_relu (mod.rs:324); cpu/src/activation.rs:92. In place. */
+int bitnet_cuda_squared_relu(bitnet_cuda_ctx* ctx, float* x, size_t len);
+
+/* Backend::softmax (mod.rs:338); cpu/src/activation.rs:230. In place. */
+int bitnet_cuda_softmax(bitnet_cuda_ctx* ctx, float* x, size_t len);
+
+/* Backend::elementwise_mul (mod.rs:350); cpu/src/lib.rs:400-420. */
+int bitnet_cuda_elementwise_mul(bitnet_cuda_ctx* ctx, const float* a, size_t a_len, const float* b, size_t b_len,
+                                float* out, size_t out_len);
+
+/* Backend::lm_head_matmul_into (mod.rs:372-383); cpu/src/lib.rs:426-447. */
+int bitnet_cuda_lm_head_matmul_into(bitnet_cuda_ctx* ctx, const float* hidden, size_t hidden_len,
+                                    const float* weights, size_t weights_len, float* output, size_t output_len,
+                                    size_t vocab_size, size_t hidden_size);
+
+/* Backend::lm_head_matmul_bf16_into (mod.rs:399-420); cpu/src/lib.rs:455-488.
+ * weights are raw bf16 bit patterns. */
+int bitnet_cuda_lm_head_matmul_bf16_into(bitnet_cuda_ctx* ctx, const float* hidden, size_t hidden_len,
+                                         const uint16_t* weights_bf16, size_t weights_len, float* output,
+                                         size_t output_len, size_t vocab_size, size_t hidden_size);
+
+/* Backend::sqrelu_gate (mod.rs:432-444); cpu/src/lib.rs:494-509. */
+int bitnet_cuda_sqrelu_gate(bitnet_cuda_ctx* ctx, const float* gate, size_t gate_len, const float* up, size_t up_len,
+                            float* out, size_t out_len);
+
+/* Backend::ternary_gemv_preq (mod.rs:459-468); cpu/src/lib.rs:519-538 -> gemv.rs:251-311.
+ * out[i] = (sum_j W[i,j]*x_q[j]) as f32 * (weight_scale*act_absmax/127). */
+int bitnet_cuda_ternary_gemv_preq(bitnet_cuda_ctx* ctx, const uint8_t* weight_packed, size_t weight_len,
+                                  float weight_scale, const int8_t* activation_q, size_t activation_len,
+                                  float act_absmax, float* output, size_t output_len, size_t out_features,
+                                  size_t in_features);
+
+/* Backend::lm_head_matmul_i8_into (mod.rs:486-509); cpu/src/lib.rs:544-575. */
+int bitnet_cuda_lm_head_matmul_i8_into(bitnet_cuda_ctx* ctx, const float* hidden, size_t hidden_len,
+                                       const int8_t* weights_i8, size_t weights_len, const float* scales,
+                                       size_t scales_len, float* output, size_t output_len, size_t vocab_size,
+                                       size_t hidden_size);
+
+/* ---- hot-path helpers that the reference calls outside the trait ---- */
+
+/* absmax_quantize_row_into (crates/bitnet-core/src/quant/absmax.rs:127-165):
+ * the model quantises once per projection group (model/src/lib.rs:957-962). */
+int bitnet_cuda_absmax_quantize_row(bitnet_cuda_ctx* ctx, const float* x, size_t len, int8_t* out, size_t out_len,
+                                    float* scale);
+
+/* ternary_gemv_preq that also returns the int32 accumulators
+ * (gemv.rs:299-308 `acc`), for bit-exact parity checks. acc may be NULL. */
+int bitnet_cuda_ternary_gemv_preq_acc(bitnet_cuda_ctx* ctx, const uint8_t* weight_packed, size_t weight_len,
+                                      float weight_scale, const int8_t* activation_q, size_t activation_len,
+                                      float act_absmax, float* output, size_t output_len, int32_t* acc,
+                                      size_t out_features, size_t in_features);
+
+/* Greedy sample_next_token (crates/bitnet-inference/src/lib.rs:263-274):
+ * argmax with ties resolved to the last index, NaN comparing Equal. */
+int bitnet_cuda_greedy_argmax(bitnet_cuda_ctx* ctx, const float* logits, size_t len, uint32_t* token);
+
+/* ===================================================================== */
+/* Device-resident ternary matmul (op sweep, composition)                 */
+/* ===================================================================== */
+
+/* Upload one TernaryWeight (crates/bitnet-core/src/quant/ternary.rs:82-91):
+ * rows*ceil(cols/4) bytes in the reference's 2-bit format; it is repacked once
+ * into the device layout. */
+int bitnet_cuda_weight_upload(bitnet_cuda_ctx* ctx, const uint8_t* packed, size_t packed_len, size_t rows,
+                              size_t cols, float scale, bitnet_cuda_weight** out);
+void bitnet_cuda_weight_destroy(bitnet_cuda_weight* w);
+
+/* Per-token absmax quantisation of M rows (absmax.rs:127-165 per row):
+ * x: device f32 [M][K] (row stride K) or bf16 when x_is_bf16 != 0.
+ * xq: device int8 [M][ldq] (ldq >= K, multiple of 64; tail zero-filled),
+ * act_absmax: device f32 [M] (the `scale*127` value the model passes on),
+ * row_sum: device int32 [M] (sum of xq, used by the matmul),
+ * status: device int32 (set non-zero if a row holds a non-finite value). */
+int bitnet_cuda_quantize_rows_device(bitnet_cuda_ctx* ctx, const void* x, int x_is_bf16, size_t M, size_t K,
+                                     int8_t* xq, size_t ldq, float* act_absmax, int32_t* row_sum, int32_t* status,
+                                     void* stream);
+
+/* out[m][n] = (sum_k W[n,k] xq[m][k]) * (scale * act_absmax[m] / 127), the
+ * batched form of ternary_gemv_quantised (gemv.rs:251-311).  acc (optional)
+ * receives the int32 accumulators [M][N]. */
+int bitnet_cuda_ternary_matmul_device(bitnet_cuda_ctx* ctx, const bitnet_cuda_weight* w, const int8_t* xq,
+                                      size_t ldq, const float* act_absmax, const int32_t* row_sum, size_t M,
+                                      float* out, int32_t* acc, void* stream);
+
+/* ===================================================================== */
+/* Device-resident model, paged KV cache, forward / decode / generate     */
+/* ===================================================================== */
+
+/* ModelConfig (crates/bitnet-core/src/config.rs:26-62). */
+typedef struct {
+  uint32_t vocab_size;
+  uint32_t hidden_size;
+  uint32_t num_hidden_layers;
+  uint32_t num_attention_heads;
+  uint32_t num_key_value_heads;
+  uint32_t intermediate_size;
+  uint32_t max_position_embeddings;
+  float rope_theta;
+  float rms_norm_eps;
+} bitnet_cuda_config;
+
+/* LayerWeights (crates/bitnet-weights/src/loader.rs:121-203): packed ternary
+ * projections in the reference format plus their per-tensor scales. */
+typedef struct {
+  const uint8_t *q_proj, *k_proj, *v_proj, *o_proj, *gate_proj, *up_proj, *down_proj;
+  float q_scale, k_scale, v_scale, o_scale, gate_scale, up_scale, down_scale;
+  const float *attention_norm, *attn_sub_norm, *ffn_norm, *ffn_sub_norm;
+} bitnet_cuda_layer_weights;
+
+/* ModelWeights (loader.rs:241-283): bf16 embedding (raw bits), the i8 lm_head
+ * (loader.rs:297-340, weight-tied to the embedding) and its per-row scales. */
+typedef struct {
+  const uint16_t* embed_tokens;
+  const int8_t* lm_head_i8;
+  const float* lm_head_scales;
+  const float* final_norm;
+  const bitnet_cuda_layer_weights* layers; /* num_hidden_layers entries */
+} bitnet_cuda_weights;
+
+/* BitNetModel::new (crates/bitnet-model/src/lib.rs:462-500): validates the
+ * config (config.rs:110-150) and uploads every tensor once. max_batch_tokens
+ * bounds the tokens of one forward (decode batch or packed prefill). */
+int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* config, const bitnet_cuda_weights* w,
+                             uint32_t max_batch_tokens, bitnet_cuda_model** out);
+void bitnet_cuda_model_destroy(bitnet_cuda_model* model);
+
+#define BITNET_KV_F32 0  /* the reference KVCache element type (model/src/lib.rs:118-169) */
+#define BITNET_KV_BF16 1 /* paged bf16 cache */
+
+/* Paged KV cache (replaces KVCache, model/src/lib.rs:118-315): num_pages pages
+ * of 16 positions x all layers, shared by up to max_seqs sequences. */
+int bitnet_cuda_kv_create(bitnet_cuda_model* model, uint32_t num_pages, uint32_t max_seqs, int kv_dtype,
+                          bitnet_cuda_kv** out);
+void bitnet_cuda_kv_destroy(bitnet_cuda_kv* kv);
+/* KVCache::clear for one sequence (frees its pages). */
+int bitnet_cuda_kv_seq_reset(bitnet_cuda_kv* kv, uint32_t seq);
+/* KVCache::len for one sequence. */
+int bitnet_cuda_kv_seq_len(bitnet_cuda_kv* kv, uint32_t seq, size_t* len);
+/* Number of free pages. */
+int bitnet_cuda_kv_free_pages(bitnet_cuda_kv* kv, size_t* n);
+/* Seed positions [0, n) of sequence seq from host K/V laid out
+ * [layer][pos][n_kv_heads*head_dim] (f32; rounded to bf16 for a bf16 cache). */
+int bitnet_cuda_kv_seq_write(bitnet_cuda_kv* kv, uint32_t seq, size_t n, const float* k, const float* v);
+/* Read positions [0, n) of sequence seq back in the same layout. */
+int bitnet_cuda_kv_seq_read(bitnet_cuda_kv* kv, uint32_t seq, size_t n, float* k, float* v);
+/* Seed positions [0, n) with seeded N(0,1) values, generated on the device
+ * (continuous-batching benchmark contexts). */
+int bitnet_cuda_kv_seq_fill_random(bitnet_cuda_kv* kv, uint32_t seq, size_t n, uint64_t seed);
+/* Reserve pages so that sequence seq can grow to `len` positions without
+ * further allocation (device-resident decode loops). */
+int bitnet_cuda_kv_seq_reserve(bitnet_cuda_kv* kv, uint32_t seq, size_t len);
+
+/* BitNetModel::forward_into (model/src/lib.rs:880-1170) for one sequence:
+ * tokens are processed at positions start_pos.. (must equal the sequence's
+ * current length); logits (host, vocab_size) receive the last token's logits. */
+int bitnet_cuda_forward(bitnet_cuda_model* model, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* tokens,
+                        size_t n_tokens, size_t start_pos, float* logits);
+
+/* One decode step for `batch` sequences (one new token each, at each
+ * sequence's current length).  logits (host [batch][vocab], may be NULL) and
+ * next_tokens (host [batch], greedy argmax, may be NULL) are outputs. */
+int bitnet_cuda_decode_step(bitnet_cuda_model* model, bitnet_cuda_kv* kv, size_t batch, const uint32_t* seq_ids,
+                            const uint32_t* tokens, float* logits, uint32_t* next_tokens);
+
+/* Device-resident decode step: seq_ids on the host (scheduler state),
+ * tokens / next_tokens / logits in device memory.  next_tokens may alias
+ * tokens.  Runs as one CUDA graph per batch size. */
+int bitnet_cuda_decode_step_device(bitnet_cuda_model* model, bitnet_cuda_kv* kv, size_t batch,
+                                   const uint32_t* seq_ids, const uint32_t* d_tokens, uint32_t* d_next_tokens,
+                                   float* d_logits, void* stream);
+
+/* Ragged prefill of n_seqs sequences packed back to back (tokens of sequence
+ * i are tokens[cu_seqlens[i] .. cu_seqlens[i+1])), appended at each
+ * sequence's current length.  logits (host [n_seqs][vocab], may be NULL) and
+ * next_tokens (host [n_seqs], may be NULL) are for each sequence's last token. */
+int bitnet_cuda_prefill(bitnet_cuda_model* model, bitnet_cuda_kv* kv, size_t n_seqs, const uint32_t* seq_ids,
+                        const uint32_t* tokens, const uint32_t* cu_seqlens, float* logits, uint32_t* next_tokens);
+
+/* generate_from_tokens_streaming (crates/bitnet-inference/src/lib.rs:701-777)
+ * with greedy sampling: clear the sequence, prefill the prompt, then decode
+ * until max_new tokens or eos0/eos1.  out_tokens holds up to max_new ids. */
+int bitnet_cuda_generate(bitnet_cuda_model* model, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* prompt,
+                         size_t n_prompt, size_t max_new, uint32_t eos0, uint32_t eos1, uint32_t* out_tokens,
+                         size_t* n_out);
+
+/* Per-kernel-class device timing of device-resident decode steps.  When
+ * enabled, decode graphs captured afterwards record CUDA events around every
+ * kernel launch; bitnet_cuda_model_kernel_times then returns, for the most
+ * recent timed step, the summed device time (ms) and the launch count of each
+ * class: [0] attention, [1] ternary matmul, [2] RMSNorm+quantise,
+ * [3] RoPE + KV store, [4] lm_head, [5] other.  Arrays hold 6 entries. */
+int bitnet_cuda_model_set_kernel_timing(bitnet_cuda_model* model, int enable);
+int bitnet_cuda_model_kernel_times(bitnet_cuda_model* model, float* ms, int32_t* launches);
+
+/* Synchronise the model's stream and report (then clear) a non-finite
+ * activation (QuantizationError) or out-of-range token id (InvalidShape) seen
+ * by device-resident steps since the last check. */
+int bitnet_cuda_model_check(bitnet_cuda_model* model);
+
+/* Number of kernels this library launched on the context (all entry points,
+ * graph-launched kernels included). */
+uint64_t bitnet_cuda_kernel_launches(const bitnet_cuda_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BITNET_CUDA_H */

@@ -1,0 +1,224 @@
+"""Model-level parity of the device-resident forward (C ABI) against the CPU
+oracle's restatement of BitNetModel::forward / generate.
+
+Tolerance: every op except attention is bit-exact, and attention's exp may
+differ from glibc expf in the last ulp, so logits are compared with
+|gpu - ref| <= 1e-3 * max|ref| (well inside the north-star 1e-2 relative)
+and greedy tokens must be identical."""
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from bitnetrs_b200 import KV_BF16, KV_F32, BitNetModel, ModelConfig, bitnet_2b_config, tiny_config
+from bitnetrs_b200 import synth
+from kat_runner import by_fn
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+
+
+def close_logits(a, b, tol=LOGIT_TOL):
+    scale = float(np.max(np.abs(b)))
+    err = float(np.max(np.abs(a - b)))
+    assert err <= tol * scale, f"max |diff| {err} > {tol} * {scale}"
+
+
+@pytest.fixture(scope="module")
+def small():
+    cfg = ModelConfig(1000, 256, 3, 8, 2, 512, 256, 500000.0, 1e-5)
+    w = synth.random_model(cfg, seed=11)
+    return cfg, w
+
+
+@pytest.fixture(scope="module")
+def small_hd128():
+    cfg = ModelConfig(777, 512, 2, 4, 1, 640, 600, 10000.0, 1e-5)
+    w = synth.random_model(cfg, seed=5)
+    return cfg, w
+
+
+@pytest.mark.parametrize("k", by_fn("tiny_model"), ids=lambda k: k["name"])
+def test_tiny_golden(cuda_backend, k):
+    w = synth.tiny_reference_model(tiny_config())
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=8)
+    kv = m.new_kv_cache(num_pages=4)
+    logits = m.forward(k["tokens"], 0, kv)
+    np.testing.assert_allclose(logits, k["logits"], atol=k["tol"], rtol=0)
+    om = O.OracleModel(w)
+    okv = om.kv(32)
+    np.testing.assert_array_equal(logits, om.forward(okv, k["tokens"], 0))
+    assert kv.len() == len(k["tokens"])
+
+
+@pytest.mark.parametrize("which", ["small", "small_hd128"])
+def test_forward_prefill_then_decode(cuda_backend, request, which):
+    cfg, w = request.getfixturevalue(which)
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
+    kv = m.new_kv_cache(num_pages=64)
+    om = O.OracleModel(w)
+    okv = om.kv(cfg.max_position_embeddings)
+    toks = synth.uniform_u32(3, 7, 40, 0, cfg.vocab_size - 1).tolist()
+    g = m.forward(toks[:30], 0, kv)
+    r = om.forward(okv, toks[:30], 0)
+    close_logits(g, r)
+    assert int(np.argmax(g)) == int(np.argmax(r))
+    for i in range(30, 40):
+        g = m.forward([toks[i]], i, kv)
+        r = om.forward(okv, [toks[i]], i)
+        close_logits(g, r)
+    assert kv.len() == 40
+
+
+def test_greedy_generate_identical(cuda_backend, small):
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
+    kv = m.new_kv_cache(num_pages=32)
+    om = O.OracleModel(w)
+    okv = om.kv(cfg.max_position_embeddings)
+    prompt = synth.uniform_u32(5, 9, 24, 0, cfg.vocab_size - 1).tolist()
+    got = m.generate(kv, prompt, 40)
+    ref, margins = om.generate(okv, prompt, 40)
+    assert got == ref, f"first divergence at {next(i for i, (a, b) in enumerate(zip(got, ref)) if a != b)}"
+
+
+def test_long_prompt_chunked_prefill(cuda_backend, small):
+    """Prompts longer than max_batch_tokens run as chunks with the same per-token math."""
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=16)
+    kv = m.new_kv_cache(num_pages=32)
+    om = O.OracleModel(w)
+    okv = om.kv(cfg.max_position_embeddings)
+    toks = synth.uniform_u32(8, 1, 50, 0, cfg.vocab_size - 1).tolist()
+    close_logits(m.forward(toks, 0, kv), om.forward(okv, toks, 0))
+
+
+@pytest.mark.parametrize("kv_dtype", [KV_F32, KV_BF16])
+def test_batched_decode_and_ragged_prefill(cuda_backend, small, kv_dtype):
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=128)
+    kv = m.new_kv_cache(num_pages=64, max_seqs=6, kv_dtype=kv_dtype)
+    om = O.OracleModel(w)
+    lens = [5, 17, 1, 33]
+    seqs = [0, 3, 4, 5]
+    prompts = [synth.uniform_u32(20 + i, 2, n, 0, cfg.vocab_size - 1).tolist() for i, n in enumerate(lens)]
+    nxt, logits = m.prefill(kv, seqs, prompts, want_logits=True)
+    okvs = [om.kv(cfg.max_position_embeddings, bf16=(kv_dtype == KV_BF16)) for _ in seqs]
+    for i in range(len(seqs)):
+        r = om.forward(okvs[i], prompts[i], 0)
+        close_logits(logits[i], r)
+        assert nxt[i] == O.lib().orc_greedy_argmax(O.p(r), r.size)
+    toks = nxt.copy()
+    for step in range(6):
+        nxt, logits = m.decode_step(kv, seqs, toks, want_logits=True)
+        for i in range(len(seqs)):
+            r = om.forward(okvs[i], [int(toks[i])], lens[i] + step)
+            close_logits(logits[i], r)
+        toks = nxt
+    for i, s in enumerate(seqs):
+        assert kv.len(s) == lens[i] + 6
+
+
+def test_seeded_context_decode(cuda_backend, small):
+    """Decode on top of an externally seeded (e.g. restored) context."""
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=16)
+    kv = m.new_kv_cache(num_pages=64, max_seqs=2, kv_dtype=KV_BF16)
+    om = O.OracleModel(w)
+    n = 70
+    k, v = synth.kv_normal(4, 1, cfg, n)
+    kv.write(1, k, v)
+    okv = om.kv(cfg.max_position_embeddings, bf16=True)
+    okv.seed(k, v)
+    kk, vv = kv.read(1, n)
+    np.testing.assert_array_equal(kk, synth.bf16_bits_to_f32(synth.f32_to_bf16_bits(k)).reshape(kk.shape))
+    tok = [123]
+    for step in range(4):
+        nxt, logits = m.decode_step(kv, [1], tok, want_logits=True)
+        r = om.forward(okv, tok, n + step)
+        close_logits(logits[0], r)
+        tok = [int(nxt[0])]
+
+
+def test_device_fill_random_matches_host_generator(cuda_backend, small):
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=16)
+    kv = m.new_kv_cache(num_pages=16, max_seqs=3, kv_dtype=KV_F32)
+    kv.fill_random(2, 40, seed=99)
+    k, v = kv.read(2, 40)
+    hk, hv = synth.kv_normal(99, 2, cfg, 40)
+    np.testing.assert_allclose(k, hk, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(v, hv, rtol=1e-6, atol=1e-6)
+
+
+def test_device_decode_graph_matches_host_path(cuda_backend, small):
+    import torch
+
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
+    kv1 = m.new_kv_cache(num_pages=64, max_seqs=4, kv_dtype=KV_BF16)
+    kv2 = m.new_kv_cache(num_pages=64, max_seqs=4, kv_dtype=KV_BF16)
+    seqs = [0, 1, 2, 3]
+    prompts = [synth.uniform_u32(40 + i, 3, 6 + 5 * i, 0, cfg.vocab_size - 1).tolist() for i in range(4)]
+    n1, _ = m.prefill(kv1, seqs, prompts)
+    n2, _ = m.prefill(kv2, seqs, prompts)
+    np.testing.assert_array_equal(n1, n2)
+    dev = torch.device("cuda", cuda_backend.device_id)
+    d_tok = torch.tensor(n2.astype(np.int64), dtype=torch.int32, device=dev)
+    d_logits = torch.empty((4, cfg.vocab_size), dtype=torch.float32, device=dev)
+    host_tok = n1
+    for step in range(5):
+        host_tok, hl = m.decode_step(kv1, seqs, host_tok, want_logits=True)
+        m.decode_step_device(kv2, seqs, d_tok.data_ptr(), d_tok.data_ptr(), d_logits.data_ptr())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(d_tok.cpu().numpy().astype(np.uint32), host_tok)
+        np.testing.assert_array_equal(d_logits.cpu().numpy(), hl)
+    m.check()
+
+
+def test_errors(cuda_backend, small):
+    from bitnetrs_b200 import BackendError, InvalidConfig, InvalidShape
+
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=8)
+    kv = m.new_kv_cache(num_pages=2, max_seqs=1)
+    with pytest.raises(InvalidShape):  # tokens must not be empty
+        m.forward([], 0, kv)
+    with pytest.raises(InvalidShape):  # gap in the cache
+        m.forward([1], 5, kv)
+    with pytest.raises(InvalidShape):  # token id >= vocab
+        m.forward([cfg.vocab_size + 3], 0, kv)
+    kv.clear()
+    with pytest.raises(BackendError):  # 2 pages = 32 positions
+        m.forward(list(range(8)) * 5, 0, kv)
+    with pytest.raises(InvalidConfig):  # hidden 12 not divisible by 5 heads (config.rs:110-150)
+        _raise_invalid_config(cuda_backend)
+
+
+def _raise_invalid_config(backend):
+    import ctypes as C
+
+    from bitnetrs_b200 import _native as N
+
+    cfg = N.Config(10, 12, 1, 5, 1, 8, 8, 10000.0, 1e-5)
+    h = C.c_void_p()
+    layers = (N.LayerWeights * 1)()
+    wts = N.Weights(None, None, None, None, layers)
+    N.check(N.cuda_lib().bitnet_cuda_model_create(backend.handle, C.byref(cfg), C.byref(wts), 8, C.byref(h)))
+
+
+def test_2b_greedy_decode_token_identical(cuda_backend):
+    """2B architecture, random init, 128-token seeded
+    prompt, 128 greedy tokens, batch 1 — tokens identical to the reference."""
+    cfg = bitnet_2b_config()
+    w = synth.random_model(cfg, seed=0)
+    prompt = synth.uniform_u32(0, 2, 128, 0, cfg.vocab_size - 1).tolist()
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=256)
+    kv = m.new_kv_cache(num_pages=32)
+    got = m.generate(kv, prompt, 128)
+    om = O.OracleModel(w)
+    okv = om.kv(cfg.max_position_embeddings)
+    ref, margins = om.generate(okv, prompt, 128)
+    assert len(ref) == 128
+    assert got == ref, (f"diverged at {next(i for i, (a, b) in enumerate(zip(got, ref)) if a != b)}; "
+                        f"min top-2 margin {float(np.min(margins)):.3g}")
