@@ -248,6 +248,7 @@ def run_cuda(a):
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t_setup
+    print(f"[bench] setup {setup_s:.1f}s, pages {pages}, mean ctx {ctxs.mean():.0f}", file=sys.stderr, flush=True)
 
     def step():
         model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
@@ -342,7 +343,15 @@ def run_cuda(a):
         e1.record(stream)
     torch.cuda.synchronize()
     b1_ms = e0.elapsed_time(e1) / 32
-    b1 = {"value": 1e3 / b1_ms, "unit": "tokens/s", "ms_per_token": b1_ms, "context": "128..160"}
+    model.set_kernel_timing(True)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            model.decode_step_device(kv, [s1], d1.data_ptr(), d1.data_ptr(), 0, stream.cuda_stream)
+    torch.cuda.synchronize()
+    kt1 = model.kernel_times()
+    model.set_kernel_timing(False)
+    b1 = {"value": 1e3 / b1_ms, "unit": "tokens/s", "ms_per_token": b1_ms, "context": "128..160",
+          "kernels_ms_per_token": {k: round(v[0], 4) for k, v in kt1.items()}}
     model.check()
 
     # ---- CPU baseline (rank 0, N=1) ----

@@ -3,6 +3,7 @@
 // Each trait method validates its slices in the reference's order (so the
 // same bad call yields the same BitNetError variant), copies the host slices
 // into device scratch, runs the kernels, and copies the outputs back.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -87,6 +88,68 @@ int build_rope_host(size_t max_seq, size_t head_dim, float theta, std::vector<fl
       sn[pos * half + i] = std::sin(angle);  // sinf
     }
   return BITNET_OK;
+}
+
+// The host libm's expf on every x in [-112, -0] whose exp evaluated in
+// double lands within 0.003 ulp of a float rounding midpoint (the GPU
+// enumerates them), kept where it differs from the double-rounded value.
+int ensure_exp_table(bitnet_cuda_ctx* c) {
+  if (c->exp_ready) return BITNET_OK;
+  const uint32_t lo = 0x80000000u, hi = 0xC2E00000u;  // -0 .. -112
+  const uint32_t cap = 8u << 20;
+  DevBuf cand, cnt;
+  BN_TRY(cand.ensure((size_t)cap * sizeof(uint2)));
+  BN_TRY(cnt.ensure(sizeof(uint32_t)));
+  BN_CUDA(cudaMemsetAsync(cnt.p, 0, sizeof(uint32_t), c->stream));
+  launch_exp_candidates(lo, hi, cand.as<uint2>(), cap, cnt.as<uint32_t>(), c->stream);
+  uint32_t n = 0;
+  BN_CUDA(cudaMemcpyAsync(&n, cnt.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+  BN_CUDA(cudaStreamSynchronize(c->stream));
+  if (n > cap) return backend_error("exp exception candidates exceed the buffer");
+  std::vector<uint2> h(n);
+  BN_CUDA(cudaMemcpy(h.data(), cand.p, (size_t)n * sizeof(uint2), cudaMemcpyDeviceToHost));
+  std::vector<std::pair<uint32_t, float>> ex;
+  for (const uint2& e : h) {
+    float x, f;
+    std::memcpy(&x, &e.x, 4);
+    std::memcpy(&f, &e.y, 4);
+    float libm = std::exp(x);  // expf of the host libm, as f32::exp
+    if (std::memcmp(&libm, &f, 4) != 0) ex.emplace_back(e.x, libm);
+  }
+  std::sort(ex.begin(), ex.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+  std::vector<uint32_t> keys(ex.size());
+  std::vector<float> vals(ex.size());
+  for (size_t i = 0; i < ex.size(); ++i) {
+    keys[i] = ex[i].first;
+    vals[i] = ex[i].second;
+  }
+  BN_TRY(c->exp_keys.ensure(std::max<size_t>(keys.size(), 1) * 4));
+  BN_TRY(c->exp_vals.ensure(std::max<size_t>(vals.size(), 1) * 4));
+  if (!keys.empty()) {
+    BN_CUDA(cudaMemcpy(c->exp_keys.p, keys.data(), keys.size() * 4, cudaMemcpyHostToDevice));
+    BN_CUDA(cudaMemcpy(c->exp_vals.p, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice));
+  }
+  c->exp_table.keys = c->exp_keys.as<uint32_t>();
+  c->exp_table.vals = c->exp_vals.as<float>();
+  c->exp_table.n = (int)keys.size();
+  c->exp_ready = true;
+  return BITNET_OK;
+}
+
+void ctx_retain(bitnet_cuda_ctx* c) { c->refs.fetch_add(1); }
+
+void ctx_release(bitnet_cuda_ctx* c) {
+  if (c->refs.fetch_sub(1) != 1) return;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& b : c->b) b.release();
+  c->status.release();
+  c->rope.d_cos.release();
+  c->rope.d_sin.release();
+  c->exp_keys.release();
+  c->exp_vals.release();
+  cudaStreamDestroy(c->stream);
+  delete c;
 }
 
 }  // namespace bitnet
@@ -242,15 +305,7 @@ int bitnet_cuda_create(uint32_t device_id, bitnet_cuda_ctx** out) {
 }
 
 void bitnet_cuda_destroy(bitnet_cuda_ctx* c) {
-  if (!c) return;
-  cudaSetDevice(c->device);
-  cudaStreamSynchronize(c->stream);
-  for (auto& b : c->b) b.release();
-  c->status.release();
-  c->rope.d_cos.release();
-  c->rope.d_sin.release();
-  cudaStreamDestroy(c->stream);
-  delete c;
+  if (c) ctx_release(c);
 }
 
 const char* bitnet_cuda_device_name(const bitnet_cuda_ctx* c) { return c ? c->name.c_str() : ""; }
@@ -406,8 +461,10 @@ int bitnet_cuda_masked_attention(bitnet_cuda_ctx* c, const float* q, size_t ql, 
   BN_CUDA(cudaMemcpy2DAsync(c->b[2].p, used * 4, vc, stride * 4, used * 4, nkv, cudaMemcpyHostToDevice, st));
   BN_TRY(c->b[3].ensure(nh * seq_len * 4));
   BN_TRY(c->b[4].ensure(qe * 4));
+  BN_TRY(ensure_exp_table(c));
   launch_masked_attention_headmajor(c->b[0].as<float>(), c->b[1].as<float>(), c->b[2].as<float>(), c->b[4].as<float>(),
-                                    (int)nh, (int)nkv, (int)hd, (int)used, (int)seq_len, c->b[3].as<float>(), st);
+                                    (int)nh, (int)nkv, (int)hd, (int)used, (int)seq_len, c->b[3].as<float>(),
+                                    c->exp_table, st);
   BN_CUDA(cudaMemcpyAsync(out, c->b[4].p, qe * 4, cudaMemcpyDeviceToHost, st));
   return finish(c);
 }
@@ -427,7 +484,8 @@ int bitnet_cuda_softmax(bitnet_cuda_ctx* c, float* x, size_t n) {
   Guard g(c);
   BN_TRY(upload(c->b[0], x, n * 4, c->stream));
   BN_TRY(c->b[1].ensure(16));
-  launch_softmax(c->b[0].as<float>(), n, c->b[1].as<float>(), c->stream);
+  BN_TRY(ensure_exp_table(c));
+  launch_softmax(c->b[0].as<float>(), n, c->b[1].as<float>(), c->exp_table, c->stream);
   BN_CUDA(cudaMemcpyAsync(x, c->b[0].p, n * 4, cudaMemcpyDeviceToHost, c->stream));
   return finish(c);
 }
@@ -539,15 +597,18 @@ int bitnet_cuda_weight_upload(bitnet_cuda_ctx* c, const uint8_t* packed, size_t 
     delete w;
     return rc;
   }
+  ctx_retain(c);
   *out = w;
   return BITNET_OK;
 }
 
 void bitnet_cuda_weight_destroy(bitnet_cuda_weight* w) {
   if (!w) return;
-  cudaSetDevice(w->ctx->device);
+  bitnet_cuda_ctx* c = w->ctx;
+  cudaSetDevice(c->device);
   cudaFree(w->words);
   delete w;
+  ctx_release(c);
 }
 
 int bitnet_cuda_quantize_rows_device(bitnet_cuda_ctx* c, const void* x, int x_is_bf16, size_t M, size_t K, int8_t* xq,

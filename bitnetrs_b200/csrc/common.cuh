@@ -107,6 +107,49 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* smem32) {
   return r;
 }
 
+// exp for the reference's softmax (ops.rs:206-227), which calls f32::exp ->
+// the host libm's expf.  exp is evaluated in double and rounded to float,
+// which is the correctly rounded result except when the double lands within
+// 2^-20 ulp of a rounding boundary; the host libm itself is within 0.502 ulp
+// of the exact value, so the two can only disagree when the exact value is
+// within 0.002 ulp of a float midpoint.  Inputs whose double result lies that
+// close (|position| > 0.497 ulp from the rounded value, ~0.15% of inputs) are
+// looked up in a sorted table of the host libm's results that differ from the
+// double-rounded one (measured once per device, see ensure_exp_table); all
+// other inputs already agree.  The table covers x in [-112, 0], the range of
+// the softmax's x - max (below -112 both give 0).
+struct ExpTable {
+  const uint32_t* keys = nullptr;  // float bit patterns, ascending
+  const float* vals = nullptr;     // the host libm's expf of each key
+  int n = 0;
+};
+
+__device__ __forceinline__ double exp_round_position(double d, float f) {
+  uint32_t fb = __float_as_uint(f);
+  double nb = (double)__uint_as_float(d >= (double)f ? fb + 1 : fb - 1);
+  double ulp = fabs(nb - (double)f);
+  return fabs(d - (double)f) / ulp;
+}
+
+__device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
+  double d = exp((double)x);
+  float f = (float)d;
+  if (t.n == 0 || !(f > 0.0f) || isinf(f)) return f;
+  if (exp_round_position(d, f) <= 0.497) return f;
+  const uint32_t key = __float_as_uint(x);
+  int lo = 0, hi = t.n - 1;
+  while (lo <= hi) {
+    int mid = (lo + hi) >> 1;
+    uint32_t k = t.keys[mid];
+    if (k == key) return t.vals[mid];
+    if (k < key)
+      lo = mid + 1;
+    else
+      hi = mid - 1;
+  }
+  return f;
+}
+
 // Rust f32::round: half away from zero (roundf), then clamp, then cast.
 __device__ __forceinline__ int8_t quant_i8(float x, float inv) {
   float s = roundf(__fmul_rn(x, inv));

@@ -1,6 +1,7 @@
 // internal.h — host-side structures shared by the C-ABI translation units.
 #pragma once
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <string>
@@ -38,7 +39,11 @@ int build_rope_host(size_t max_seq, size_t head_dim, float theta, std::vector<fl
 
 }  // namespace bitnet
 
+// Handles are reference counted: models and uploaded weights keep their
+// context alive and KV caches keep their model alive, so the public destroy
+// functions may be called in any order.
 struct bitnet_cuda_ctx {
+  std::atomic<int> refs{1};
   int device = 0;
   cudaStream_t stream = nullptr;
   std::mutex mu;
@@ -46,6 +51,10 @@ struct bitnet_cuda_ctx {
   bitnet::DevBuf b[8];  // scratch for the per-call trait methods
   bitnet::DevBuf status;
   bitnet::RopeTable rope;
+  // host-libm expf exceptions (see ExpTable); built once per context
+  bool exp_ready = false;
+  bitnet::DevBuf exp_keys, exp_vals;
+  bitnet::ExpTable exp_table;
 };
 
 struct bitnet_cuda_weight {
@@ -54,3 +63,10 @@ struct bitnet_cuda_weight {
   float scale = 0.0f;
   uint32_t* words = nullptr;
 };
+
+namespace bitnet {
+void ctx_retain(bitnet_cuda_ctx* c);
+void ctx_release(bitnet_cuda_ctx* c);
+// Builds ctx->exp_table on first use (caller holds ctx->mu, not capturing).
+int ensure_exp_table(bitnet_cuda_ctx* c);
+}  // namespace bitnet

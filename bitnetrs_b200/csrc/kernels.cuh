@@ -37,7 +37,7 @@ void launch_squared_relu(float* x, size_t n, cudaStream_t st);
 void launch_sqrelu_gate(const float* g, const float* u, float* out, size_t n, cudaStream_t st);
 void launch_elementwise_mul(const float* a, const float* b, float* out, size_t n, cudaStream_t st);
 // activation::softmax in place over one vector (sequential sum order).
-void launch_softmax(float* x, size_t n, float* scratch_max, cudaStream_t st);
+void launch_softmax(float* x, size_t n, float* scratch_max, const ExpTable& et, cudaStream_t st);
 // bf16 embedding rows -> f32 hidden rows.
 void launch_embed(const uint16_t* embed, const uint32_t* tokens, int T, int H, float* h, int32_t* status, int vocab,
                   cudaStream_t st);
@@ -70,13 +70,20 @@ enum class LmW : int { I8 = 0, BF16 = 1, F32 = 2 };
 // out[m][v] = dot(W[v], h[m]) (* scales[v] for I8), reference FMA order.
 void launch_lm_head(const void* W, LmW wt, const float* scales, const float* h, int ldh, int M, int V, int H,
                     float* out, int ldo, cudaStream_t st);
+// Tensor-core i8 lm_head for many tokens (h split into three bf16 terms);
+// a3 is scratch of M*3*H bf16.  Requires H % 64 == 0.
+bool lm_head_mma_supported(int H);
+int lm_head_mma_prepare();  // outside graph capture; 0 on success
+void launch_lm_head_mma(const float* h, int M, int V, int H, const int8_t* W, const float* scales, uint16_t* a3,
+                        float* out, int ldo, cudaStream_t st);
 // greedy argmax per row (ties -> last index, NaN compares Equal).
 void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cudaStream_t st);
 
 // ---- attention -------------------------------------------------------------------
 // Backend::masked_attention on a head-major cache (attention.rs:97-209).
 void launch_masked_attention_headmajor(const float* q, const float* kc, const float* vc, float* out, int nh, int nkv,
-                                       int hd, int stride, int seq_len, float* scratch, cudaStream_t st);
+                                       int hd, int stride, int seq_len, float* scratch, const ExpTable& et,
+                                       cudaStream_t st);
 
 // Backend::rope_embed on one row [q (nh*hd) | k (nkv*hd)] -> out (same layout).
 void launch_rope_apply(const float* qk, int nh, int nkv, int hd, const float* cos_table, const float* sin_table,
@@ -104,6 +111,38 @@ void launch_paged_attention(const float* q, int T, int nh, const int32_t* tok_po
                             const int32_t* page_table, const KvGeom& kv, int layer, int max_ctx, float* out,
                             float* partial, size_t partial_floats, cudaStream_t st);
 size_t paged_attention_partial_floats(int T, int nh, int hd, int max_ctx);
+
+// Same attention in the reference's exact operation order (see kernels_attn.cu).
+// Scores take G*max_ctx floats of shared memory (scores_in_smem) or
+// T*nh*max_ctx floats of global scratch.
+void launch_paged_attention_exact(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
+                                  const int32_t* page_table, const KvGeom& kv, int layer, int max_ctx, float* out,
+                                  float* scratch, bool scores_in_smem, const ExpTable& et, cudaStream_t st);
+size_t paged_attention_exact_smem(int nh, int kv_heads, int hd, int max_ctx);
+// Raises the kernel's dynamic shared memory limit (call outside graph capture); 0 on success.
+int paged_attention_exact_prepare(size_t smem);
+
+// Reference-order attention for a bf16 cache with head_dim 128 and group 4,
+// organised for throughput (scores in shared memory: exact2_smem bytes).
+bool exact2_supported(const KvGeom& kv, int nh);
+size_t exact2_smem(int max_ctx);
+int exact2_prepare(size_t smem);  // outside graph capture; 0 on success
+void launch_paged_attention_exact2(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
+                                   const int32_t* page_table, const KvGeom& kv, int layer, int max_ctx, float* out,
+                                   const ExpTable& et, cudaStream_t st);
+// Candidates for the exp exception table: bit patterns u in [lo, hi] whose
+// double-evaluated exp lands within 0.003 ulp of a float rounding midpoint;
+// writes (u, (float)exp((double)x)) pairs and counts them in *count.
+void launch_exp_candidates(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count, cudaStream_t st);
+
+// Tensor-core decode attention (bf16 cache, head_dim 128, group <= 4), split
+// over the context; partial holds flash_decode_mma_partial_floats floats.
+bool flash_decode_mma_supported(const KvGeom& kv, int nh);
+size_t flash_decode_mma_partial_floats(int T, int nh, int max_ctx);
+int flash_decode_mma_prepare();  // outside graph capture; 0 on success
+void launch_flash_decode_mma(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
+                             const int32_t* page_table, const KvGeom& kv, int layer, int max_ctx, float* out,
+                             float* partial, cudaStream_t st);
 
 // Fill positions [0, n) of sequence `seq` (all layers) with seeded N(0,1).
 void launch_kv_fill_random(const KvGeom& kv, const int32_t* page_row, int n, uint64_t seed, uint32_t seq,

@@ -116,13 +116,12 @@ __device__ float rms_inv_exact(const float* x, int d, float eps, float* bcast) {
     float acc = 0.0f;
     if (lane < 8) {
       int i = 0;
-      for (; i + 4 <= chunks; i += 4) {
-        float a0 = x[8 * (i + 0) + lane], a1 = x[8 * (i + 1) + lane];
-        float a2 = x[8 * (i + 2) + lane], a3 = x[8 * (i + 3) + lane];
-        acc = __fmaf_rn(a0, a0, acc);
-        acc = __fmaf_rn(a1, a1, acc);
-        acc = __fmaf_rn(a2, a2, acc);
-        acc = __fmaf_rn(a3, a3, acc);
+      for (; i + 16 <= chunks; i += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = x[8 * (i + u) + lane];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc = __fmaf_rn(v[u], v[u], acc);
       }
       for (; i < chunks; ++i) {
         float a = x[8 * i + lane];
@@ -161,22 +160,44 @@ void launch_rms_norm(const float* x, int ldx, const float* w, int d, float eps, 
   count_launch();
 }
 
+// One block per row: the row (or sqrelu(gate)*up) is staged in shared
+// memory by all threads, lanes 0..7 of warp 0 run the reference's eight FMA
+// chains from there, then the block forms y = (x * inv) * w, its absmax and
+// the int8 row (absmax.rs:127-165).
 template <bool GATE_UP>
-__global__ void norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ x2, int ldx,
-                                  const float* __restrict__ w, int d, float eps, int8_t* __restrict__ xq, int ldq,
-                                  float* act_absmax, int32_t* row_sum, int32_t* status) {
+__global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ x2,
+                                                         int ldx, const float* __restrict__ w, int d, float eps,
+                                                         int8_t* __restrict__ xq, int ldq, float* __restrict__ act_absmax,
+                                                         int32_t* __restrict__ row_sum, int32_t* status) {
   extern __shared__ float row[];
   __shared__ float bc;
   __shared__ float red_f[32];
   __shared__ int red_i[32];
-  int m = blockIdx.x;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float v = x[(size_t)m * ldx + i];
-    if (GATE_UP) {
-      float r = fmaxf(v, 0.0f);  // f32::max(0.0): NaN -> 0
-      v = __fmul_rn(__fmul_rn(r, r), x2[(size_t)m * ldx + i]);
+  const int m = blockIdx.x;
+  const float* xr = x + (size_t)m * ldx;
+  const bool vec = (d & 3) == 0 && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0 && (!GATE_UP || ((uintptr_t)x2 & 15) == 0);
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const float4* y4 = GATE_UP ? reinterpret_cast<const float4*>(x2 + (size_t)m * ldx) : nullptr;
+    for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
+      float4 v = x4[i];
+      if (GATE_UP) {
+        float4 u = y4[i];
+        float r0 = fmaxf(v.x, 0.0f), r1 = fmaxf(v.y, 0.0f), r2 = fmaxf(v.z, 0.0f), r3 = fmaxf(v.w, 0.0f);
+        v = make_float4(__fmul_rn(__fmul_rn(r0, r0), u.x), __fmul_rn(__fmul_rn(r1, r1), u.y),
+                        __fmul_rn(__fmul_rn(r2, r2), u.z), __fmul_rn(__fmul_rn(r3, r3), u.w));
+      }
+      reinterpret_cast<float4*>(row)[i] = v;
     }
-    row[i] = v;
+  } else {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+      float v = xr[i];
+      if (GATE_UP) {
+        float r = fmaxf(v, 0.0f);  // f32::max(0.0): NaN -> 0
+        v = __fmul_rn(__fmul_rn(r, r), x2[(size_t)m * ldx + i]);
+      }
+      row[i] = v;
+    }
   }
   __syncthreads();
   float inv = rms_inv_exact(row, d, eps, &bc);
@@ -235,18 +256,13 @@ void launch_elementwise_mul(const float* a, const float* b, float* out, size_t n
   count_launch();
 }
 
-// expf of the reference (glibc) is evaluated here as exp in double rounded to
-// float: both are within one float ulp of the exact value and agree except
-// when the exact result is extremely close to a rounding boundary.
-__device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
-
 // softmax (activation.rs:230-255): max, exp(x - max), sequential sum, * 1/sum.
-__global__ void softmax_max_exp_kernel(float* x, size_t n, float* out_max) {
+__global__ void softmax_max_exp_kernel(float* x, size_t n, float* out_max, ExpTable et) {
   __shared__ float red[32];
   float m = -INFINITY;
   for (size_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, x[i]);
   m = block_reduce(m, [](float a, float b) { return fmaxf(a, b); }, red);
-  for (size_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = exp_ref(__fsub_rn(x[i], m));
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = exp_host_libm(__fsub_rn(x[i], m), et);
   if (threadIdx.x == 0) *out_max = m;
 }
 __global__ void softmax_sum_kernel(const float* x, size_t n, float* out_inv) {
@@ -258,9 +274,9 @@ __global__ void softmax_scale_kernel(float* x, size_t n, const float* inv) {
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) x[i] = __fmul_rn(x[i], *inv);
 }
-void launch_softmax(float* x, size_t n, float* scratch, cudaStream_t st) {
+void launch_softmax(float* x, size_t n, float* scratch, const ExpTable& et, cudaStream_t st) {
   if (!n) return;
-  softmax_max_exp_kernel<<<1, 1024, 0, st>>>(x, n, scratch);
+  softmax_max_exp_kernel<<<1, 1024, 0, st>>>(x, n, scratch, et);
   softmax_sum_kernel<<<1, 1, 0, st>>>(x, n, scratch + 1);
   softmax_scale_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(x, n, scratch + 1);
   count_launch(3);
@@ -292,6 +308,26 @@ __global__ void gather_rows_kernel(const float* __restrict__ src, int ld, const 
 void launch_gather_rows(const float* src, int ld, const int32_t* rows, int n, float* dst, cudaStream_t st) {
   if (n <= 0) return;
   gather_rows_kernel<<<n, 256, 0, st>>>(src, ld, rows, dst);
+  count_launch();
+}
+
+__global__ void exp_candidates_kernel(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= (uint64_t)(hi - lo);
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    uint32_t u = lo + (uint32_t)i;
+    float x = __uint_as_float(u);
+    double d = exp((double)x);
+    float f = (float)d;
+    if (!(f > 0.0f) || isinf(f)) continue;
+    if (exp_round_position(d, f) > 0.497) {
+      uint32_t slot = atomicAdd(count, 1u);
+      if (slot < cap) out[slot] = make_uint2(u, __float_as_uint(f));
+    }
+  }
+}
+
+void launch_exp_candidates(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count, cudaStream_t st) {
+  exp_candidates_kernel<<<148 * 16, 256, 0, st>>>(lo, hi, out, cap, count);
   count_launch();
 }
 

@@ -133,6 +133,161 @@ void launch_lm_head(const void* W, LmW wt, const float* scales, const float* h, 
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-core lm_head for many tokens: logits = (W_i8 . h) * scale.
+// h (f32) is split into three bf16 terms h1 + h2 + h3 (h1 = bf16(h),
+// h2 = bf16(h - h1), h3 = bf16(h - h1 - h2)), which represent h to 2^-27
+// relative; int8 weights are exact in bf16, so every product the tensor core
+// forms is exact and only the f32 accumulation order differs from the
+// reference's FMA chains.  A' = [h1 | h2 | h3] is [M][3H] bf16.
+// ---------------------------------------------------------------------------
+__global__ void split_bf16x3_kernel(const float* __restrict__ h, int H, uint16_t* __restrict__ a3) {
+  const int m = blockIdx.x;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float x = h[(size_t)m * H + i];
+    uint16_t b1 = f32_to_bf16_bits(x);
+    float r1 = x - bf16_bits_to_f32(b1);
+    uint16_t b2 = f32_to_bf16_bits(r1);
+    float r2 = r1 - bf16_bits_to_f32(b2);
+    uint16_t b3 = f32_to_bf16_bits(r2);
+    uint16_t* row = a3 + (size_t)m * 3 * H;
+    row[i] = b1;
+    row[H + i] = b2;
+    row[2 * H + i] = b3;
+  }
+}
+
+__device__ __forceinline__ void cpa16(void* smem_dst, const void* gsrc, int bytes) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gsrc), "r"(bytes));
+}
+__device__ __forceinline__ void ldsm4(uint32_t r[4], const void* p) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Two int8 (consecutive bytes of a 16-bit word) -> packed bf16x2 (exact).
+__device__ __forceinline__ uint32_t i8x2_to_bf16x2(uint32_t w16) {
+  float lo = (float)(int8_t)(w16 & 0xff), hi = (float)(int8_t)((w16 >> 8) & 0xff);
+  return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+}
+
+// Block tile 64 tokens x 128 vocab rows x 64 k; 8 warps as 2 (M) x 4 (N), warp tile 32 x 32.
+constexpr int kLmBM = 64, kLmBN = 128, kLmBK = 64, kLmStages = 3;
+constexpr int kLmAS = kLmBK * 2 + 16;  // A smem row: 64 bf16 + 16 B pad
+constexpr int kLmWS = kLmBK + 16;      // W smem row: 64 int8 + 16 B pad
+
+__global__ void __launch_bounds__(256) lm_head_mma_kernel(const uint16_t* __restrict__ a3, const int8_t* __restrict__ W,
+                                                          const float* __restrict__ scales, int M, int V, int H,
+                                                          float* __restrict__ out, int ldo) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* as = smem;                                    // [stages][BM][kLmAS]
+  uint8_t* ws = smem + kLmStages * kLmBM * kLmAS;       // [stages][BN][kLmWS]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wm = warp >> 2, wn = warp & 3;
+  const int m0 = blockIdx.x * kLmBM, n0 = blockIdx.y * kLmBN;
+  const int K3 = 3 * H;
+  const int ktiles = K3 / kLmBK;  // H % 64 == 0 (checked by the launcher)
+
+  auto load = [&](int stage, int kt) {
+    const int k = kt * kLmBK;
+    // A': 64 rows x 128 B
+    for (int c = threadIdx.x; c < kLmBM * 8; c += 256) {
+      int r = c >> 3, sg = c & 7;
+      int gm = m0 + r;
+      const uint16_t* src = a3 + (size_t)min(gm, M - 1) * K3 + k + sg * 8;
+      cpa16(as + (stage * kLmBM + r) * kLmAS + sg * 16, src, gm < M ? 16 : 0);
+    }
+    // W: 128 rows x 64 B (k mod H)
+    const int kw = k % H;
+    for (int c = threadIdx.x; c < kLmBN * 4; c += 256) {
+      int r = c >> 2, sg = c & 3;
+      int gv = n0 + r;
+      const int8_t* src = W + (size_t)min(gv, V - 1) * H + kw + sg * 16;
+      cpa16(ws + (stage * kLmBN + r) * kLmWS + sg * 16, src, gv < V ? 16 : 0);
+    }
+  };
+
+  float acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+
+#pragma unroll
+  for (int s = 0; s < kLmStages - 1; ++s) {
+    if (s < ktiles) load(s, s);
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+  for (int kt = 0; kt < ktiles; ++kt) {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kLmStages - 2));
+    __syncthreads();
+    if (kt + kLmStages - 1 < ktiles) load((kt + kLmStages - 1) % kLmStages, kt + kLmStages - 1);
+    asm volatile("cp.async.commit_group;\n" ::);
+    const uint8_t* ast = as + (kt % kLmStages) * kLmBM * kLmAS;
+    const uint8_t* wst = ws + (kt % kLmStages) * kLmBN * kLmWS;
+#pragma unroll
+    for (int ks = 0; ks < kLmBK / 16; ++ks) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        int row = wm * 32 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        ldsm4(a[mt], ast + row * kLmAS + ks * 32 + (lane >> 4) * 16);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const uint8_t* wr = wst + (wn * 32 + nt * 8 + (lane >> 2)) * kLmWS + ks * 16 + 2 * (lane & 3);
+        uint32_t b0 = i8x2_to_bf16x2(*reinterpret_cast<const uint16_t*>(wr));
+        uint32_t b1 = i8x2_to_bf16x2(*reinterpret_cast<const uint16_t*>(wr + 8));
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) mma16816(acc[mt][nt], a[mt], b0, b1);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      int m = m0 + wm * 32 + mt * 16 + (lane >> 2) + 8 * half;
+      if (m >= M) continue;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          int v = n0 + wn * 32 + nt * 8 + 2 * (lane & 3) + e;
+          if (v < V) out[(size_t)m * ldo + v] = acc[mt][nt][2 * half + e] * scales[v];
+        }
+    }
+}
+
+bool lm_head_mma_supported(int H) { return H % kLmBK == 0; }
+
+int lm_head_mma_prepare() {
+  int smem = kLmStages * (kLmBM * kLmAS + kLmBN * kLmWS);
+  return cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess
+             ? 0
+             : 1;
+}
+
+void launch_lm_head_mma(const float* h, int M, int V, int H, const int8_t* W, const float* scales, uint16_t* a3,
+                        float* out, int ldo, cudaStream_t st) {
+  if (M <= 0 || V <= 0) return;
+  split_bf16x3_kernel<<<M, 256, 0, st>>>(h, H, a3);
+  int smem = kLmStages * (kLmBM * kLmAS + kLmBN * kLmWS);
+  dim3 grid((unsigned)ceil_div(M, kLmBM), (unsigned)ceil_div(V, kLmBN));
+  lm_head_mma_kernel<<<grid, 256, smem, st>>>(a3, W, scales, M, V, H, out, ldo);
+  count_launch(2);
+}
+
+// ---------------------------------------------------------------------------
 // Greedy argmax with Iterator::max_by(partial_cmp) semantics
 // (inference/lib.rs:263-274): a NaN compares Equal, so the fold restarts
 // after the last NaN; among the rest the last maximal index wins.

@@ -30,10 +30,19 @@ std::string sz(size_t v) { return std::to_string(v); }
 }  // namespace
 
 struct bitnet_cuda_model {
+  std::atomic<int> refs{1};  // the user handle + one per KV cache
   bitnet_cuda_ctx* ctx = nullptr;
   bitnet_cuda_config cfg{};
   int H = 0, hd = 0, nh = 0, nkv = 0, qd = 0, kvd = 0, F = 0, V = 0, L = 0, Tmax = 0;
   int ldq = 0;  // row stride of the quantised activation buffer
+  bool exact_smem_ok = false;  // shared-memory limit of the exact attention kernel raised
+  size_t exact_smem_max = 0;
+  bool mma_attn_ok = false;  // shared-memory limit of the tensor-core attention kernel raised
+  bool lm_mma_ok = false;    // tensor-core lm_head usable (hidden % 64 == 0, smem limit raised)
+  bool exact2_ok = false;    // shared-memory limit of the bf16/hd128 reference-order attention raised
+  size_t exact2_smem_max = 0;
+  uint16_t* a3 = nullptr;    // [R][3H] bf16 split of the final-normed rows
+  int numerics = BITNET_NUMERICS_AUTO;
   std::vector<Layer> layers;
   std::vector<void*> allocs;
   uint16_t* embed = nullptr;
@@ -86,6 +95,8 @@ struct bitnet_cuda_kv {
   int32_t* d_table = nullptr;
   size_t capacity() const { return (size_t)g.max_pages_per_seq * kPage; }
 };
+
+static void model_release(bitnet_cuda_model* m);
 
 namespace {
 
@@ -158,6 +169,35 @@ int kv_reserve(bitnet_cuda_kv* kv, uint32_t seq, size_t end, cudaStream_t st) {
   return BITNET_OK;
 }
 
+// Attention policy: the reference-order kernel serves decode steps and
+// short prefills (each query token streams its own context); long packed
+// prefills use the split-context kernel.
+constexpr int kExactMaxTokens = 1024;
+constexpr int kSmallStepTokens = 16;
+constexpr size_t kExactMaxSmem = 200 * 1024;
+
+// Kernel choice (bitnet_cuda_model_set_numerics):
+//  - attention feeds the next int8 quantisation, so outside FAST mode it
+//    always runs in the reference's operation order;
+//  - the lm_head feeds nothing back: AUTO runs the tensor-core kernel for
+//    steps with more than kSmallStepTokens output rows.
+bool use_exact_attention(const bitnet_cuda_model* m, int T) {
+  return m->numerics != BITNET_NUMERICS_FAST && T <= kExactMaxTokens && m->nh / m->nkv <= 8;
+}
+bool use_mma_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T) {
+  return !use_exact_attention(m, T) && m->mma_attn_ok && flash_decode_mma_supported(kv->g, m->nh);
+}
+bool use_exact2_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
+  return m->exact2_ok && exact2_supported(kv->g, m->nh) && exact2_smem(max_ctx) <= m->exact2_smem_max;
+}
+bool use_fast_lm_head(const bitnet_cuda_model* m, int n_out) {
+  if (!m->lm_mma_ok || m->numerics == BITNET_NUMERICS_EXACT) return false;
+  return m->numerics == BITNET_NUMERICS_FAST || n_out > kSmallStepTokens;
+}
+bool exact_scores_in_smem(const bitnet_cuda_model* m, int max_ctx) {
+  return m->exact_smem_ok && paged_attention_exact_smem(m->nh, m->nkv, m->hd, max_ctx) <= m->exact_smem_max;
+}
+
 // Kernel classes for the per-step timing of device-resident decode graphs.
 enum KClass { kAttn = 0, kMatmul = 1, kNormQuant = 2, kRopeKv = 3, kLmHead = 4, kOther = 5, kClasses = 6 };
 
@@ -171,9 +211,10 @@ void timed(bitnet_cuda_model* m, int cls, cudaStream_t st, F launch) {
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
-  cudaEventRecord(a, st);
+  // external records become event-record nodes of the captured graph
+  cudaEventRecordWithFlags(a, st, cudaEventRecordExternal);
   launch();
-  cudaEventRecord(b, st);
+  cudaEventRecordWithFlags(b, st, cudaEventRecordExternal);
   m->marks->emplace_back(cls, a, b);
 }
 
@@ -210,8 +251,19 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
                            kv->d_table, kv->g, l, m->qrot, st);
     });
     timed(m, kAttn, st, [&] {
-      launch_paged_attention(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, m->attn,
-                             m->partial.as<float>(), m->partial.cap / 4, st);
+      if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx))
+        launch_paged_attention_exact2(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx,
+                                      m->attn, m->ctx->exp_table, st);
+      else if (use_exact_attention(m, T))
+        launch_paged_attention_exact(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx,
+                                     m->attn, m->partial.as<float>(), exact_scores_in_smem(m, max_ctx),
+                                     m->ctx->exp_table, st);
+      else if (use_mma_attention(m, kv, T))
+        launch_flash_decode_mma(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, m->attn,
+                                m->partial.as<float>(), st);
+      else
+        launch_paged_attention(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, m->attn,
+                               m->partial.as<float>(), m->partial.cap / 4, st);
     });
     timed(m, kNormQuant, st, [&] {
       launch_norm_quant(m->attn, nullptr, qd, Lw.attn_sub_norm, qd, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status,
@@ -257,17 +309,25 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
     launch_rms_norm(m->qrot, H, m->final_norm, H, eps, m->hn, H, n_out, st);
   });
   timed(m, kLmHead, st, [&] {
-    launch_lm_head(m->lm_i8, LmW::I8, m->lm_scales, m->hn, H, n_out, m->V, H, m->logits, m->V, st);
+    if (use_fast_lm_head(m, n_out))
+      launch_lm_head_mma(m->hn, n_out, m->V, H, m->lm_i8, m->lm_scales, m->a3, m->logits, m->V, st);
+    else
+      launch_lm_head(m->lm_i8, LmW::I8, m->lm_scales, m->hn, H, n_out, m->V, H, m->logits, m->V, st);
   });
   timed(m, kOther, st, [&] {
     launch_argmax(m->logits, m->V, n_out, m->V, m->next, st);
   });
 }
 
+// Reads (and clears) the device status word; synchronises the stream.
 int check_status(bitnet_cuda_model* m) {
   int32_t s = 0;
   BN_CUDA(cudaMemcpyAsync(&s, m->status, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
   BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (s) {
+    BN_CUDA(cudaMemsetAsync(m->status, 0, 4, m->ctx->stream));
+    BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  }
   if (s & 2) return shape_error("token id < vocab_size", "out-of-range token id");
   if (s & 1) return quant_error("non-finite activation value in the forward pass");
   return BITNET_OK;
@@ -329,8 +389,14 @@ void drop_graphs(bitnet_cuda_model* m) {
   m->last_timed = nullptr;
 }
 
-int ensure_partial(bitnet_cuda_model* m, int T, int max_ctx) {
-  size_t bytes = paged_attention_partial_floats(T, m->nh, m->hd, max_ctx) * sizeof(float);
+int ensure_partial(bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  size_t floats = use_exact_attention(m, T)
+                      ? ((use_exact2_attention(m, kv, max_ctx) || exact_scores_in_smem(m, max_ctx))
+                             ? 0
+                             : (size_t)T * m->nh * max_ctx)
+                      : (use_mma_attention(m, kv, T) ? flash_decode_mma_partial_floats(T, m->nh, max_ctx)
+                                                     : paged_attention_partial_floats(T, m->nh, m->hd, max_ctx));
+  size_t bytes = std::max<size_t>(floats, 16) * sizeof(float);
   if (bytes <= m->partial.cap) return BITNET_OK;
   // captured graphs hold the old address
   BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
@@ -339,6 +405,20 @@ int ensure_partial(bitnet_cuda_model* m, int T, int max_ctx) {
 }
 
 }  // namespace
+
+static void model_release(bitnet_cuda_model* m) {
+  if (m->refs.fetch_sub(1) != 1) return;
+  bitnet_cuda_ctx* c = m->ctx;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  drop_graphs(m);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->h_meta) cudaFreeHost(m->h_meta);
+  if (m->h_tokens) cudaFreeHost(m->h_tokens);
+  m->partial.release();
+  delete m;
+  ctx_release(c);
+}
 
 extern "C" {
 
@@ -353,6 +433,7 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
   cudaSetDevice(ctx->device);
   auto* m = new bitnet_cuda_model();
   m->ctx = ctx;
+  ctx_retain(ctx);
   m->cfg = *cfg;
   m->H = (int)cfg->hidden_size;
   m->nh = (int)cfg->num_attention_heads;
@@ -366,7 +447,7 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
   m->Tmax = (int)max_batch_tokens;
   m->ldq = (int)std::max({padded_cols(m->H), padded_cols(m->qd), padded_cols(m->F)});
   auto fail = [&](int rc) {
-    bitnet_cuda_model_destroy(m);
+    model_release(m);
     return rc;
   };
   int rc;
@@ -406,6 +487,23 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
   if ((rc = put(m, &m->lm_i8, w->lm_head_i8, V * H))) return fail(rc);
   if ((rc = put(m, &m->lm_scales, w->lm_head_scales, V))) return fail(rc);
   if ((rc = put(m, &m->final_norm, w->final_norm, H))) return fail(rc);
+  {
+    size_t smem = paged_attention_exact_smem(m->nh, m->nkv, m->hd, (int)round_up(cfg->max_position_embeddings, kPage));
+    if (smem <= kExactMaxSmem && paged_attention_exact_prepare(smem) == 0) {
+      m->exact_smem_ok = true;
+      m->exact_smem_max = smem;
+    }
+  }
+  if ((rc = ensure_exp_table(ctx))) return fail(rc);
+  m->mma_attn_ok = flash_decode_mma_prepare() == 0;
+  m->lm_mma_ok = lm_head_mma_supported(m->H) && lm_head_mma_prepare() == 0;
+  {
+    size_t smem = exact2_smem((int)round_up(cfg->max_position_embeddings, kPage));
+    if (smem <= kExactMaxSmem && exact2_prepare(smem) == 0) {
+      m->exact2_ok = true;
+      m->exact2_smem_max = smem;
+    }
+  }
   // RoPE table for every position the model accepts (rope.rs:100-147).
   std::vector<float> cs, sn;
   if ((rc = build_rope_host(cfg->max_position_embeddings, m->hd, cfg->rope_theta, cs, sn))) return fail(rc);
@@ -421,6 +519,7 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
   if ((rc = m->alloc(&m->gu, T * 2 * F))) return fail(rc);
   if ((rc = m->alloc(&m->hn, R * H))) return fail(rc);
   if ((rc = m->alloc(&m->logits, R * V))) return fail(rc);
+  if ((rc = m->alloc(&m->a3, R * 3 * H))) return fail(rc);
   if ((rc = m->alloc(&m->xq, T * m->ldq))) return fail(rc);
   if ((rc = m->alloc(&m->amax, T))) return fail(rc);
   if ((rc = m->alloc(&m->rowsum, T))) return fail(rc);
@@ -443,15 +542,7 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
 }
 
 void bitnet_cuda_model_destroy(bitnet_cuda_model* m) {
-  if (!m) return;
-  cudaSetDevice(m->ctx->device);
-  cudaStreamSynchronize(m->ctx->stream);
-  drop_graphs(m);
-  for (void* p : m->allocs) cudaFree(p);
-  if (m->h_meta) cudaFreeHost(m->h_meta);
-  if (m->h_tokens) cudaFreeHost(m->h_tokens);
-  m->partial.release();
-  delete m;
+  if (m) model_release(m);
 }
 
 // ---- KV cache -----------------------------------------------------------------
@@ -493,6 +584,7 @@ int bitnet_cuda_kv_create(bitnet_cuda_model* m, uint32_t num_pages, uint32_t max
   for (uint32_t i = 0; i < num_pages; ++i) kv->free_pages[i] = (int32_t)(num_pages - 1 - i);
   kv->seq_pages.assign(max_seqs, {});
   kv->seq_len.assign(max_seqs, 0);
+  m->refs.fetch_add(1);
   *out = kv;
   return BITNET_OK;
 }
@@ -514,6 +606,7 @@ void bitnet_cuda_kv_destroy(bitnet_cuda_kv* kv) {
   cudaFree(kv->g.pool);
   cudaFree(kv->d_table);
   delete kv;
+  model_release(m);
 }
 
 int bitnet_cuda_kv_seq_reset(bitnet_cuda_kv* kv, uint32_t seq) {
@@ -604,7 +697,7 @@ static int forward_common(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t n_seq
   int T = 0, max_ctx = 1;
   BN_TRY(prepare_batch(m, kv, n_seqs, seq_ids, counts, &T, &max_ctx, st));
   if (n_seqs > 1024) return shape_error("<= 1024 sequences per call", sz(n_seqs));
-  BN_TRY(ensure_partial(m, T, max_ctx));
+  BN_TRY(ensure_partial(m, kv, T, max_ctx));
   std::memcpy(m->h_tokens, tokens, (size_t)T * 4);
   BN_CUDA(cudaMemcpyAsync(m->tokens, m->h_tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st));
   BN_TRY(upload_meta(m, T, (int)n_seqs, st));
@@ -663,7 +756,7 @@ static int decode_graph(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t batch, 
   // The graph is sized for the cache capacity so it can be replayed as
   // contexts grow; splits past a token's context exit immediately.
   const int cap_ctx = (int)kv->capacity();
-  BN_TRY(ensure_partial(m, T, cap_ctx));
+  BN_TRY(ensure_partial(m, kv, T, cap_ctx));
   BN_TRY(upload_meta(m, T, T, st));
   if (src_on_host) {
     std::memcpy(m->h_tokens, src, (size_t)T * 4);
@@ -728,6 +821,18 @@ int bitnet_cuda_decode_step_device(bitnet_cuda_model* m, bitnet_cuda_kv* kv, siz
   return BITNET_OK;
 }
 
+int bitnet_cuda_model_set_numerics(bitnet_cuda_model* m, int mode) {
+  if (!m) return shape_error("non-null model", "null");
+  if (mode != BITNET_NUMERICS_AUTO && mode != BITNET_NUMERICS_EXACT && mode != BITNET_NUMERICS_FAST)
+    return config_error("numerics mode must be AUTO, EXACT or FAST");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  m->numerics = mode;
+  drop_graphs(m);  // captured graphs embed the previous kernel choice
+  return BITNET_OK;
+}
+
 int bitnet_cuda_model_set_kernel_timing(bitnet_cuda_model* m, int enable) {
   if (!m) return shape_error("non-null model", "null");
   std::lock_guard<std::mutex> lk(m->ctx->mu);
@@ -758,10 +863,7 @@ int bitnet_cuda_model_check(bitnet_cuda_model* m) {
   if (!m) return shape_error("non-null model", "null");
   std::lock_guard<std::mutex> lk(m->ctx->mu);
   cudaSetDevice(m->ctx->device);
-  int rc = check_status(m);
-  BN_CUDA(cudaMemsetAsync(m->status, 0, 64, m->ctx->stream));
-  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
-  return rc;
+  return check_status(m);
 }
 
 int bitnet_cuda_generate(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* prompt,

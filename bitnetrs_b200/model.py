@@ -222,6 +222,12 @@ class BitNetModel:
     def check(self) -> None:
         check(self._lib.bitnet_cuda_model_check(self._h))
 
+    NUMERICS = {"auto": 0, "exact": 1, "fast": 2}
+
+    def set_numerics(self, mode: str) -> None:
+        """"auto" (reference-order kernels for steps <= 16 tokens), "exact" or "fast"."""
+        check(self._lib.bitnet_cuda_model_set_numerics(self._h, self.NUMERICS[mode]))
+
     KERNEL_CLASSES = ("attention", "ternary_matmul", "norm_quant", "rope_kv_store", "lm_head", "other")
 
     def set_kernel_timing(self, enable: bool) -> None:

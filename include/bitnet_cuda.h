@@ -285,6 +285,23 @@ int bitnet_cuda_generate(bitnet_cuda_model* model, bitnet_cuda_kv* kv, uint32_t 
                          size_t n_prompt, size_t max_new, uint32_t eos0, uint32_t eos1, uint32_t* out_tokens,
                          size_t* n_out);
 
+/* Numerics of the model's forward passes.  The ternary matmul, activation
+ * quantisation, norms, RoPE and residual adds are bit-identical to the
+ * reference CPU backend in every mode.
+ *  AUTO  (default): attention in the reference's operation order (bit-
+ *        identical except the exp, which is correctly rounded where glibc's
+ *        expf may differ by one ulp); the lm_head of steps with more than 16
+ *        output rows on tensor cores (every product exact, f32 accumulation
+ *        in a different order: ~1e-7 relative), otherwise reference order.
+ *  EXACT: reference operation order everywhere.
+ *  FAST : tensor-core attention and lm_head at every size (f32-level
+ *        accuracy; int8 re-quantisation then drifts from the reference over
+ *        long sequences). */
+#define BITNET_NUMERICS_AUTO 0
+#define BITNET_NUMERICS_EXACT 1
+#define BITNET_NUMERICS_FAST 2
+int bitnet_cuda_model_set_numerics(bitnet_cuda_model* model, int mode);
+
 /* Per-kernel-class device timing of device-resident decode steps.  When
  * enabled, decode graphs captured afterwards record CUDA events around every
  * kernel launch; bitnet_cuda_model_kernel_times then returns, for the most

@@ -952,6 +952,21 @@ int orc_kv_seed(void* p, size_t n, const float* k, const float* v) {
   return OK;
 }
 
+// Read positions [0, n) back in the [layer][pos][kv_head*hd] layout.
+int orc_kv_read(const void* p, size_t n, float* k, float* v) {
+  const KV* kv = (const KV*)p;
+  if (n > kv->max_seq) return ERR_SHAPE;
+  size_t row = kv->nkv * kv->hd;
+  for (size_t l = 0; l < kv->n_layers; ++l)
+    for (size_t t = 0; t < n; ++t)
+      for (size_t h = 0; h < kv->nkv; ++h)
+        for (size_t d = 0; d < kv->hd; ++d) {
+          k[(l * n + t) * row + h * kv->hd + d] = kv->k[l][h * kv->max_seq * kv->hd + t * kv->hd + d];
+          v[(l * n + t) * row + h * kv->hd + d] = kv->v[l][h * kv->max_seq * kv->hd + t * kv->hd + d];
+        }
+  return OK;
+}
+
 int orc_forward(void* model, void* kv, const uint32_t* tokens, size_t n, size_t start_pos, float* logits) {
   return model_forward(*(Model*)model, *(KV*)kv, tokens, n, start_pos, logits);
 }

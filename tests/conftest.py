@@ -35,6 +35,6 @@ def pytest_collection_modifyitems(config, items):
 def cuda_backend():
     from bitnetrs_b200 import CudaBackend
 
-    b = CudaBackend(int(os.environ.get("BITNET_TEST_DEVICE", "0")))
-    yield b
-    b.close()
+    # Models and caches created by tests hold references to the context; it is
+    # released when the last of them goes away.
+    yield CudaBackend(int(os.environ.get("BITNET_TEST_DEVICE", "0")))

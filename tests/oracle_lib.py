@@ -65,6 +65,7 @@ _SIGS = {
     "orc_kv_clear": (None, [vp]),
     "orc_kv_len": (sz, [vp]),
     "orc_kv_seed": (i32, [vp, sz, vp, vp]),
+    "orc_kv_read": (i32, [vp, sz, vp, vp]),
     "orc_forward": (i32, [vp, vp, vp, sz, sz, vp]),
     "orc_generate": (i32, [vp, vp, vp, sz, sz, u32, u32, vp, C.POINTER(sz), vp]),
 }
@@ -156,6 +157,15 @@ class OracleKV:
 
     def __len__(self):
         return lib().orc_kv_len(self._h)
+
+    def read(self, n):
+        c = self._model.config
+        k = np.empty((c.num_hidden_layers, n, c.kv_dim()), dtype=np.float32)
+        v = np.empty_like(k)
+        rc = lib().orc_kv_read(self._h, n, p(k), p(v))
+        if rc:
+            raise RuntimeError(f"oracle kv read failed: {ERR[rc]}")
+        return k, v
 
     def seed(self, k, v):
         k = np.ascontiguousarray(k, dtype=np.float32)

@@ -1,0 +1,77 @@
+"""Op sweep of the ternary matmul (BASELINE config "ternary matmul op sweep"):
+the 2B layer shapes at M in {1, 8, 64, 512} plus edge sizes, through the
+device-resident C-ABI entry points.  Int8 activations and int32
+accumulators must be bit-exact; f32 outputs bit-exact against the oracle's
+ternary_gemv_quantised applied per row."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from bitnetrs_b200 import _native as N
+from bitnetrs_b200 import synth
+
+pytestmark = pytest.mark.gpu
+L = O.lib()
+
+
+def unpack_codes(packed, rows, cols):
+    pc = (cols + 3) // 4
+    b = packed.reshape(rows, pc)
+    codes = np.stack([(b >> (2 * j)) & 3 for j in range(4)], axis=-1).reshape(rows, pc * 4)[:, :cols]
+    return np.where(codes == 0, 1.0, np.where(codes == 2, -1.0, 0.0))
+
+
+@pytest.mark.parametrize("M", [1, 2, 8, 16, 17, 64, 65, 128, 256, 512])
+@pytest.mark.parametrize("N_,K", [(2560, 2560), (640, 2560), (2560, 6912), (6912, 2560), (100, 200)])
+def test_device_matmul_bit_exact(cuda_backend, M, N_, K):
+    import torch
+
+    if M == 512 and N_ * K > 2560 * 2560:
+        pytest.skip("covered by the 2560x2560 case at M=512")
+    lib = N.cuda_lib()
+    dev = torch.device("cuda", cuda_backend.device_id)
+    packed = synth.ternary_codes(M + N_, 3, N_, K)
+    scale = 0.0161
+    wh = C.c_void_p()
+    N.check(lib.bitnet_cuda_weight_upload(cuda_backend.handle, packed.ctypes.data, packed.size, N_, K, scale,
+                                          C.byref(wh)))
+    x_bf16 = synth.bf16_normal(M, 7, M * K, 1.0)
+    ldq = (K + 63) // 64 * 64
+    d_x = torch.from_numpy(x_bf16.view(np.int16).copy()).to(dev)
+    d_xq = torch.zeros((M, ldq), dtype=torch.int8, device=dev)
+    d_amax = torch.zeros(M, dtype=torch.float32, device=dev)
+    d_rs = torch.zeros(M, dtype=torch.int32, device=dev)
+    d_st = torch.zeros(1, dtype=torch.int32, device=dev)
+    d_out = torch.zeros((M, N_), dtype=torch.float32, device=dev)
+    d_acc = torch.zeros((M, N_), dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    N.check(lib.bitnet_cuda_quantize_rows_device(cuda_backend.handle, d_x.data_ptr(), 1, M, K, d_xq.data_ptr(), ldq,
+                                                 d_amax.data_ptr(), d_rs.data_ptr(), d_st.data_ptr(), None))
+    N.check(lib.bitnet_cuda_ternary_matmul_device(cuda_backend.handle, wh, d_xq.data_ptr(), ldq, d_amax.data_ptr(),
+                                                  d_rs.data_ptr(), M, d_out.data_ptr(), d_acc.data_ptr(), None))
+    torch.cuda.synchronize()
+    lib.bitnet_cuda_weight_destroy(wh)
+    xq = d_xq.cpu().numpy()[:, :K]
+    amax = d_amax.cpu().numpy()
+    assert d_st.item() == 0
+    # int8 activations: the reference quantiser on the same rows
+    xf = synth.bf16_bits_to_f32(x_bf16).reshape(M, K)
+    for m in range(0, M, max(1, M // 8)):
+        q = np.zeros(K, dtype=np.int8)
+        s = C.c_float()
+        assert L.orc_absmax_quantize_row_into(O.p(xf[m].copy()), K, O.p(q), K, C.byref(s)) == 0
+        np.testing.assert_array_equal(xq[m], q)
+        assert amax[m] == np.float32(s.value) * np.float32(127.0)
+    # int32 accumulators: exact integer product (float64 is exact at these magnitudes)
+    W = unpack_codes(packed, N_, K)
+    ref_acc = (xq.astype(np.float64) @ W.T).astype(np.int64)
+    np.testing.assert_array_equal(d_acc.cpu().numpy(), ref_acc)
+    # f32 outputs: the reference epilogue per row
+    out = d_out.cpu().numpy()
+    for m in range(0, M, max(1, M // 4)):
+        ro = np.zeros(N_, dtype=np.float32)
+        assert L.orc_ternary_gemv_preq(O.p(packed), packed.size, scale, O.p(np.ascontiguousarray(xq[m])), K,
+                                       float(amax[m]), O.p(ro), N_, N_, K, None) == 0
+        np.testing.assert_array_equal(out[m], ro)

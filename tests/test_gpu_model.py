@@ -1,10 +1,11 @@
 """Model-level parity of the device-resident forward (C ABI) against the CPU
 oracle's restatement of BitNetModel::forward / generate.
 
-Tolerance: every op except attention is bit-exact, and attention's exp may
-differ from glibc expf in the last ulp, so logits are compared with
-|gpu - ref| <= 1e-3 * max|ref| (well inside the north-star 1e-2 relative)
-and greedy tokens must be identical."""
+In the reference-order numerics every op reproduces the reference bit for
+bit (the exp included, see ExpTable), so most comparisons are exact; the
+tolerance |gpu - ref| <= 1e-3 * max|ref| is kept for the tensor-core paths
+(well inside the north-star 1e-2 relative) and greedy tokens must be
+identical."""
 import numpy as np
 import pytest
 
@@ -70,6 +71,25 @@ def test_forward_prefill_then_decode(cuda_backend, request, which):
     assert kv.len() == 40
 
 
+@pytest.mark.parametrize("mode", ["auto", "exact", "fast"])
+def test_long_prefill_modes(cuda_backend, small_hd128, mode):
+    """A 128-token prompt in one step: the M=128 matmul tiles and the large-step attention path."""
+    cfg, w = small_hd128
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=256)
+    m.set_numerics(mode)
+    kv = m.new_kv_cache(num_pages=64)
+    om = O.OracleModel(w)
+    okv = om.kv(cfg.max_position_embeddings)
+    toks = synth.uniform_u32(12, 7, 128, 0, cfg.vocab_size - 1).tolist()
+    # FAST attention re-quantises slightly different activations, so its
+    # int8 roundings drift from the reference; it is held to the north-star
+    # 1e-2 bound, the reference-order modes to 1e-3.
+    tol = 1e-2 if mode == "fast" else LOGIT_TOL
+    close_logits(m.forward(toks, 0, kv), om.forward(okv, toks, 0), tol)
+    for i in range(128, 131):
+        close_logits(m.forward([toks[i - 128]], i, kv), om.forward(okv, [toks[i - 128]], i), tol)
+
+
 def test_greedy_generate_identical(cuda_backend, small):
     cfg, w = small
     m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
@@ -108,6 +128,10 @@ def test_batched_decode_and_ragged_prefill(cuda_backend, small, kv_dtype):
         r = om.forward(okvs[i], prompts[i], 0)
         close_logits(logits[i], r)
         assert nxt[i] == O.lib().orc_greedy_argmax(O.p(r), r.size)
+        gk, gv = kv.read(seqs[i], lens[i])
+        rk, rv = okvs[i].read(lens[i])
+        np.testing.assert_allclose(gk, rk, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(gv, rv, rtol=1e-4, atol=1e-5)
     toks = nxt.copy()
     for step in range(6):
         nxt, logits = m.decode_step(kv, seqs, toks, want_logits=True)
@@ -176,6 +200,45 @@ def test_device_decode_graph_matches_host_path(cuda_backend, small):
     m.check()
 
 
+@pytest.fixture(scope="module")
+def hd128():
+    # head_dim 128 with a GQA group of 4: the shape the tensor-core decode kernel serves
+    cfg = ModelConfig(3000, 512, 2, 4, 1, 768, 2048, 500000.0, 1e-5)
+    return cfg, synth.random_model(cfg, seed=21)
+
+
+@pytest.mark.parametrize("lens", [[100, 300, 513, 1000, 1, 256, 257, 1500]])
+def test_fast_numerics_one_step(cuda_backend, hd128, lens):
+    """One decode step from identical seeded state: the tensor-core attention
+    (split over 256-position chunks) and tensor-core lm_head agree with the
+    reference-order kernels and with the oracle to f32-level accuracy."""
+    cfg, w = hd128
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
+    om = O.OracleModel(w)
+    seqs = list(range(len(lens)))
+    toks = synth.uniform_u32(9, 4, len(lens), 0, cfg.vocab_size - 1).tolist()
+    ctx = [synth.kv_normal(31, s, cfg, n) for s, n in zip(seqs, lens)]
+    out = {}
+    for mode in ("exact", "fast"):
+        m.set_numerics(mode)
+        kv = m.new_kv_cache(num_pages=400, max_seqs=len(lens), kv_dtype=KV_BF16)
+        for s, (k, v) in zip(seqs, ctx):
+            kv.write(s, k, v)
+        nxt, logits = m.decode_step(kv, seqs, toks, want_logits=True)
+        out[mode] = (nxt, logits)
+        kv.close()
+    for i, s in enumerate(seqs):
+        okv = om.kv(lens[i] + 4, bf16=True)
+        okv.seed(*ctx[i])
+        r = om.forward(okv, [toks[i]], lens[i])
+        close_logits(out["exact"][1][i], r, tol=1e-5)
+        close_logits(out["fast"][1][i], r, tol=1e-3)
+        top2 = np.partition(r, -2)[-2:]
+        if top2[1] - top2[0] > 1e-3 * np.max(np.abs(r)):
+            assert out["fast"][0][i] == out["exact"][0][i]
+    m.set_numerics("auto")
+
+
 def test_errors(cuda_backend, small):
     from bitnetrs_b200 import BackendError, InvalidConfig, InvalidShape
 
@@ -209,16 +272,37 @@ def _raise_invalid_config(backend):
 
 def test_2b_greedy_decode_token_identical(cuda_backend):
     """2B architecture, random init, 128-token seeded
-    prompt, 128 greedy tokens, batch 1 — tokens identical to the reference."""
+    prompt, 128 greedy tokens at batch 1.  The oracle decodes greedily; the
+    GPU is fed the same tokens (teacher forcing) so every step's logits are
+    compared on identical inputs: logits within the north-star 1e-2 relative
+    at every step and the greedy token identical at every step."""
     cfg = bitnet_2b_config()
     w = synth.random_model(cfg, seed=0)
     prompt = synth.uniform_u32(0, 2, 128, 0, cfg.vocab_size - 1).tolist()
     m = BitNetModel(w, cuda_backend, max_batch_tokens=256)
     kv = m.new_kv_cache(num_pages=32)
-    got = m.generate(kv, prompt, 128)
     om = O.OracleModel(w)
     okv = om.kv(cfg.max_position_embeddings)
-    ref, margins = om.generate(okv, prompt, 128)
-    assert len(ref) == 128
-    assert got == ref, (f"diverged at {next(i for i, (a, b) in enumerate(zip(got, ref)) if a != b)}; "
-                        f"min top-2 margin {float(np.min(margins)):.3g}")
+    L = O.lib()
+    g = m.forward(prompt, 0, kv)
+    r = om.forward(okv, prompt, 0)
+    stats = []
+    for step in range(128):
+        tok = int(L.orc_greedy_argmax(O.p(r), r.size))
+        top2 = np.partition(r, -2)[-2:]
+        margin = float(top2[1] - top2[0])
+        err = float(np.max(np.abs(g - r)))
+        gtok = int(cuda_backend.greedy_argmax(g))
+        stats.append((step, err, margin, tok, gtok))
+        pos = len(prompt) + step
+        g = m.forward([tok], pos, kv)
+        r = om.forward(okv, [tok], pos)
+    errs = np.array([s[1] for s in stats])
+    bad = [s for s in stats if s[3] != s[4]]
+    print(f"max |dlogit| {errs.max():.3g} (median {np.median(errs):.3g}); bit-identical steps "
+          f"{int(np.sum(errs == 0))}/128; min oracle top-2 margin {min(s[2] for s in stats):.3g}; "
+          f"token mismatches {bad}")
+    assert errs.max() <= 1e-2 * float(np.max(np.abs(r)))
+    assert not bad, f"greedy token differs at {bad[:3]} (step, |dlogit|, oracle top-2 margin, ref, gpu)"
+    # every op reproduces the reference, so the logits are bit-identical
+    assert int(np.sum(errs == 0)) == 128
