@@ -299,6 +299,7 @@ def run_cuda(a):
     L, nkv, hd, H = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim(), cfg.hidden_size
     ctx_at = ctx_before + 2  # positions attended in the last timed step (incl. its own token)
     attn_bytes = float(np.sum(ctx_at) * nkv * hd * 2 * 2 + 2 * B * H * 4)
+    attn_kernel = model.attention_kernel(kv, B)
     attn_ms, attn_n = kt["attention"]
     attn_launch_ms = attn_ms / max(attn_n, 1) * 1.0
     attn_gbs = attn_bytes / (attn_launch_ms / 1e3) / 1e9 if attn_n else None
@@ -376,10 +377,10 @@ def run_cuda(a):
                                                                          f"collective)",
                        "l2": "inputs larger than L2 (~44 GB of KV read per step)"},
             "e2e": e2e,
-            "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel (decode, split-K)",
+            "roofline": {"bound": "hbm", "kernel": attn_kernel,
                          "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
                          "frac": (attn_gbs / peak) if attn_gbs else None,
-                         "traffic": traffic_from_profiles("paged_attention_kernel"),
+                         "traffic": traffic_from_profiles(attn_kernel),
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": attn_bytes,
                          "avg_launch_ms": attn_launch_ms},
             "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32, mma.sync)", "ms_per_step": mm_ms,

@@ -129,9 +129,30 @@ int ensure_exp_table(bitnet_cuda_ctx* c) {
     BN_CUDA(cudaMemcpy(c->exp_keys.p, keys.data(), keys.size() * 4, cudaMemcpyHostToDevice));
     BN_CUDA(cudaMemcpy(c->exp_vals.p, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice));
   }
+  // open-addressing copy: load factor <= 0.4, linear probing
+  uint32_t bits = 10;
+  while ((1u << bits) < keys.size() * 5 / 2) ++bits;
+  const uint32_t slots = 1u << bits;
+  std::vector<uint2> hash(slots, make_uint2(0u, 0u));
+  int probes = 0;
+  for (size_t i = 0; i < keys.size(); ++i) {
+    uint32_t j = (keys[i] * kExpHashMul) >> (32 - bits);
+    int k = 0;
+    while (hash[(j + k) & (slots - 1)].x != 0u) ++k;
+    uint32_t vb;
+    std::memcpy(&vb, &vals[i], 4);
+    hash[(j + k) & (slots - 1)] = make_uint2(keys[i], vb);
+    probes = std::max(probes, k);
+  }
+  BN_TRY(c->exp_hash.ensure((size_t)slots * sizeof(uint2)));
+  BN_CUDA(cudaMemcpy(c->exp_hash.p, hash.data(), (size_t)slots * sizeof(uint2), cudaMemcpyHostToDevice));
   c->exp_table.keys = c->exp_keys.as<uint32_t>();
   c->exp_table.vals = c->exp_vals.as<float>();
   c->exp_table.n = (int)keys.size();
+  c->exp_table.hash = c->exp_hash.as<uint2>();
+  c->exp_table.hash_shift = 32 - bits;
+  c->exp_table.hash_mask = slots - 1;
+  c->exp_table.hash_probes = probes;
   c->exp_ready = true;
   return BITNET_OK;
 }
@@ -148,6 +169,7 @@ void ctx_release(bitnet_cuda_ctx* c) {
   c->rope.d_sin.release();
   c->exp_keys.release();
   c->exp_vals.release();
+  c->exp_hash.release();
   cudaStreamDestroy(c->stream);
   delete c;
 }

@@ -114,15 +114,23 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* smem32) {
 // of the exact value, so the two can only disagree when the exact value is
 // within 0.002 ulp of a float midpoint.  Inputs whose double result lies that
 // close (|position| > 0.497 ulp from the rounded value, ~0.15% of inputs) are
-// looked up in a sorted table of the host libm's results that differ from the
+// looked up in a table of the host libm's results that differ from the
 // double-rounded one (measured once per device, see ensure_exp_table); all
 // other inputs already agree.  The table covers x in [-112, 0], the range of
-// the softmax's x - max (below -112 both give 0).
+// the softmax's x - max (below -112 both give 0).  It is held twice: sorted
+// (keys/vals, binary search) and as an open-addressing hash of (key, value)
+// pairs (linear probing, at most hash_probes slots per lookup, key 0 = empty
+// since +0.0 is never an entry).
 struct ExpTable {
   const uint32_t* keys = nullptr;  // float bit patterns, ascending
   const float* vals = nullptr;     // the host libm's expf of each key
   int n = 0;
+  const uint2* hash = nullptr;     // (key, value bits) slots
+  uint32_t hash_shift = 32;        // slot = (key * kExpHashMul) >> hash_shift
+  uint32_t hash_mask = 0;          // slots - 1
+  int hash_probes = 0;             // longest probe sequence in the table
 };
+constexpr uint32_t kExpHashMul = 0x9E3779B1u;
 
 __device__ __forceinline__ double exp_round_position(double d, float f) {
   uint32_t fb = __float_as_uint(f);
@@ -131,12 +139,28 @@ __device__ __forceinline__ double exp_round_position(double d, float f) {
   return fabs(d - (double)f) / ulp;
 }
 
-__device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
+// First half of exp_host_libm: the double-rounded value, and whether the
+// input needs the table (returns true; the caller resolves it later).
+__device__ __forceinline__ bool exp_needs_table(float x, const ExpTable& t, float* out) {
   double d = exp((double)x);
   float f = (float)d;
-  if (t.n == 0 || !(f > 0.0f) || isinf(f)) return f;
-  if (exp_round_position(d, f) <= 0.497) return f;
-  const uint32_t key = __float_as_uint(x);
+  *out = f;
+  if (t.n == 0 || !(f > 0.0f) || isinf(f)) return false;
+  return exp_round_position(d, f) > 0.497;
+}
+
+// Second half: the host libm's value for a table candidate `key` whose
+// double-rounded value is f.
+__device__ __forceinline__ float exp_table_lookup(uint32_t key, float f, const ExpTable& t) {
+  if (t.hash) {
+    uint32_t i = (key * kExpHashMul) >> t.hash_shift;
+    for (int k = 0; k <= t.hash_probes; ++k) {
+      const uint2 e = t.hash[(i + k) & t.hash_mask];
+      if (e.x == key) return __uint_as_float(e.y);
+      if (e.x == 0u) return f;
+    }
+    return f;
+  }
   int lo = 0, hi = t.n - 1;
   while (lo <= hi) {
     int mid = (lo + hi) >> 1;
@@ -148,6 +172,12 @@ __device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
       hi = mid - 1;
   }
   return f;
+}
+
+__device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
+  float f;
+  if (!exp_needs_table(x, t, &f)) return f;
+  return exp_table_lookup(__float_as_uint(x), f, t);
 }
 
 // Rust f32::round: half away from zero (roundf), then clamp, then cast.

@@ -3,7 +3,15 @@
 
 #include "common.cuh"
 
+#include <cuda.h>
+
 namespace bitnet {
+
+// Bits of the device status word (read and cleared by the host after a step).
+constexpr int kStatusNonFinite = 1;    // non-finite activation met by a quantiser
+constexpr int kStatusBadToken = 2;     // token id >= vocab_size
+constexpr int kStatusBadContext = 4;   // a token's context exceeds the kernel's capacity
+constexpr int kStatusWaitTimeout = 8;  // a bounded device-side wait gave up
 
 // Per-launch kernel counter (reported by bitnet_cuda_kernel_launches).
 void count_launch(uint64_t n = 1);
@@ -130,6 +138,15 @@ int exact2_prepare(size_t smem);  // outside graph capture; 0 on success
 void launch_paged_attention_exact2(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
                                    const int32_t* page_table, const KvGeom& kv, int layer, int max_ctx, float* out,
                                    const ExpTable& et, cudaStream_t st);
+// The same computation fed by TMA (2-D tiles, 128-byte swizzle) through a
+// ring of page slots; needs a tensor map of the pool (exact3_make_tmap).
+bool exact3_supported(const KvGeom& kv, int nh);
+size_t exact3_smem(int max_ctx);
+int exact3_prepare(size_t smem);  // outside graph capture; 0 on success
+int exact3_make_tmap(const KvGeom& kv, CUtensorMap* map);  // 0 on success
+void launch_paged_attention_exact3(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
+                                   const int32_t* page_table, const KvGeom& kv, const CUtensorMap& map, int layer,
+                                   int max_ctx, float* out, const ExpTable& et, int32_t* status, cudaStream_t st);
 // Candidates for the exp exception table: bit patterns u in [lo, hi] whose
 // double-evaluated exp lands within 0.003 ulp of a float rounding midpoint;
 // writes (u, (float)exp((double)x)) pairs and counts them in *count.

@@ -41,6 +41,8 @@ struct bitnet_cuda_model {
   bool lm_mma_ok = false;    // tensor-core lm_head usable (hidden % 64 == 0, smem limit raised)
   bool exact2_ok = false;    // shared-memory limit of the bf16/hd128 reference-order attention raised
   size_t exact2_smem_max = 0;
+  bool exact3_ok = false;    // same for the TMA-fed variant
+  size_t exact3_smem_max = 0;
   uint16_t* a3 = nullptr;    // [R][3H] bf16 split of the final-normed rows
   int numerics = BITNET_NUMERICS_AUTO;
   std::vector<Layer> layers;
@@ -93,6 +95,8 @@ struct bitnet_cuda_kv {
   std::vector<size_t> seq_len;
   std::vector<int32_t> h_table;
   int32_t* d_table = nullptr;
+  CUtensorMap tmap{};     // the pool as a tensor for TMA (bf16, head_dim 128)
+  bool tmap_ok = false;
   size_t capacity() const { return (size_t)g.max_pages_per_seq * kPage; }
 };
 
@@ -190,6 +194,9 @@ bool use_mma_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int
 bool use_exact2_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
   return m->exact2_ok && exact2_supported(kv->g, m->nh) && exact2_smem(max_ctx) <= m->exact2_smem_max;
 }
+bool use_exact3_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
+  return m->exact3_ok && kv->tmap_ok && exact3_supported(kv->g, m->nh) && exact3_smem(max_ctx) <= m->exact3_smem_max;
+}
 bool use_fast_lm_head(const bitnet_cuda_model* m, int n_out) {
   if (!m->lm_mma_ok || m->numerics == BITNET_NUMERICS_EXACT) return false;
   return m->numerics == BITNET_NUMERICS_FAST || n_out > kSmallStepTokens;
@@ -251,7 +258,10 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
                            kv->d_table, kv->g, l, m->qrot, st);
     });
     timed(m, kAttn, st, [&] {
-      if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx))
+      if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx))
+        launch_paged_attention_exact3(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, kv->tmap, l,
+                                      max_ctx, m->attn, m->ctx->exp_table, m->status, st);
+      else if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx))
         launch_paged_attention_exact2(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx,
                                       m->attn, m->ctx->exp_table, st);
       else if (use_exact_attention(m, T))
@@ -319,6 +329,15 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
   });
 }
 
+// Name of the attention kernel run_forward launches for T tokens (same tests).
+const char* attention_kernel_name(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx)) return "paged_attention_exact3_kernel";
+  if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx)) return "paged_attention_exact2_kernel";
+  if (use_exact_attention(m, T)) return "paged_attention_exact_kernel";
+  if (use_mma_attention(m, kv, T)) return "flash_decode_mma_kernel";
+  return "paged_attention_kernel";
+}
+
 // Reads (and clears) the device status word; synchronises the stream.
 int check_status(bitnet_cuda_model* m) {
   int32_t s = 0;
@@ -328,8 +347,10 @@ int check_status(bitnet_cuda_model* m) {
     BN_CUDA(cudaMemsetAsync(m->status, 0, 4, m->ctx->stream));
     BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
   }
-  if (s & 2) return shape_error("token id < vocab_size", "out-of-range token id");
-  if (s & 1) return quant_error("non-finite activation value in the forward pass");
+  if (s & kStatusWaitTimeout) return backend_error("a device-side wait timed out (attention pipeline)");
+  if (s & kStatusBadContext) return backend_error("a token's context exceeds the attention kernel's capacity");
+  if (s & kStatusBadToken) return shape_error("token id < vocab_size", "out-of-range token id");
+  if (s & kStatusNonFinite) return quant_error("non-finite activation value in the forward pass");
   return BITNET_OK;
 }
 
@@ -391,7 +412,8 @@ void drop_graphs(bitnet_cuda_model* m) {
 
 int ensure_partial(bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
   size_t floats = use_exact_attention(m, T)
-                      ? ((use_exact2_attention(m, kv, max_ctx) || exact_scores_in_smem(m, max_ctx))
+                      ? ((use_exact3_attention(m, kv, max_ctx) || use_exact2_attention(m, kv, max_ctx) ||
+                          exact_scores_in_smem(m, max_ctx))
                              ? 0
                              : (size_t)T * m->nh * max_ctx)
                       : (use_mma_attention(m, kv, T) ? flash_decode_mma_partial_floats(T, m->nh, max_ctx)
@@ -504,6 +526,13 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
       m->exact2_smem_max = smem;
     }
   }
+  {
+    size_t smem = exact3_smem((int)round_up(cfg->max_position_embeddings, kPage));
+    if (smem <= kExactMaxSmem && exact3_prepare(smem) == 0) {
+      m->exact3_ok = true;
+      m->exact3_smem_max = smem;
+    }
+  }
   // RoPE table for every position the model accepts (rope.rs:100-147).
   std::vector<float> cs, sn;
   if ((rc = build_rope_host(cfg->max_position_embeddings, m->hd, cfg->rope_theta, cs, sn))) return fail(rc);
@@ -580,6 +609,7 @@ int bitnet_cuda_kv_create(bitnet_cuda_model* m, uint32_t num_pages, uint32_t max
   cudaMemsetAsync(kv->d_table, 0, tbl * sizeof(int32_t), m->ctx->stream);
   cudaStreamSynchronize(m->ctx->stream);
   kv->h_table.assign(tbl, 0);
+  kv->tmap_ok = exact3_make_tmap(kv->g, &kv->tmap) == 0;
   kv->free_pages.resize(num_pages);
   for (uint32_t i = 0; i < num_pages; ++i) kv->free_pages[i] = (int32_t)(num_pages - 1 - i);
   kv->seq_pages.assign(max_seqs, {});
@@ -830,6 +860,16 @@ int bitnet_cuda_model_set_numerics(bitnet_cuda_model* m, int mode) {
   cudaStreamSynchronize(m->ctx->stream);
   m->numerics = mode;
   drop_graphs(m);  // captured graphs embed the previous kernel choice
+  return BITNET_OK;
+}
+
+int bitnet_cuda_model_attention_kernel(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t tokens, char* name,
+                                       size_t name_len) {
+  if (!m || !kv || !name || name_len == 0) return shape_error("non-null arguments", "null");
+  if (tokens == 0) return shape_error("tokens > 0", "0");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  const char* k = attention_kernel_name(m, kv, (int)tokens, (int)kv->capacity());
+  std::snprintf(name, name_len, "%s", k);
   return BITNET_OK;
 }
 

@@ -234,6 +234,12 @@ class BitNetModel:
         """Record CUDA events around every kernel of decode graphs captured from now on."""
         check(self._lib.bitnet_cuda_model_set_kernel_timing(self._h, 1 if enable else 0))
 
+    def attention_kernel(self, kv: "KVCache", tokens: int = 1) -> str:
+        """Name of the attention kernel a step of `tokens` query tokens over `kv` launches."""
+        buf = C.create_string_buffer(64)
+        check(self._lib.bitnet_cuda_model_attention_kernel(self._h, kv.handle, tokens, buf, 64))
+        return buf.value.decode()
+
     def kernel_times(self):
         """{class: (device ms summed over the most recent timed step, launches)}."""
         ms = np.zeros(6, dtype=np.float32)

@@ -313,8 +313,16 @@ int bitnet_cuda_model_kernel_times(bitnet_cuda_model* model, float* ms, int32_t*
 
 /* Synchronise the model's stream and report (then clear) a non-finite
  * activation (QuantizationError) or out-of-range token id (InvalidShape) seen
- * by device-resident steps since the last check. */
+ * by device-resident steps since the last check, and a device-side wait that
+ * gave up or a context beyond the attention kernel's capacity (BackendError). */
 int bitnet_cuda_model_check(bitnet_cuda_model* model);
+
+/* Diagnostics (no counterpart in the reference): writes into `name` (NUL
+ * terminated, at most name_len bytes) the name of the attention kernel that a
+ * step of `tokens` query tokens over `kv` launches under the current numerics
+ * mode, for contexts up to the cache's capacity. */
+int bitnet_cuda_model_attention_kernel(bitnet_cuda_model* model, bitnet_cuda_kv* kv, uint32_t tokens, char* name,
+                                       size_t name_len);
 
 /* Number of kernels this library launched on the context (all entry points,
  * graph-launched kernels included). */

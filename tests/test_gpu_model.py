@@ -239,6 +239,60 @@ def test_fast_numerics_one_step(cuda_backend, hd128, lens):
     m.set_numerics("auto")
 
 
+@pytest.fixture(scope="module")
+def gqa4_2kv():
+    # head_dim 128, GQA group 4, two kv heads and two layers: the shape served by
+    # the TMA-fed reference-order attention, with kv-head and layer offsets
+    cfg = ModelConfig(1500, 1024, 2, 8, 2, 512, 4200, 500000.0, 1e-5)
+    return cfg, synth.random_model(cfg, seed=33)
+
+
+# contexts around page (16) and ring (8 pages) boundaries, up to the capacity
+X3_LENS = [1, 2, 15, 16, 17, 31, 33, 127, 128, 129, 255, 1000, 2047, 4150]
+
+
+def test_reference_order_decode_bf16_hd128(cuda_backend, gqa4_2kv):
+    """One decode step over seeded bf16 contexts of many lengths: logits are
+    bit-identical to the oracle's BitNetModel::forward."""
+    cfg, w = gqa4_2kv
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
+    m.set_numerics("exact")
+    om = O.OracleModel(w)
+    seqs = list(range(len(X3_LENS)))
+    kv = m.new_kv_cache(num_pages=sum(n // 16 + 2 for n in X3_LENS), max_seqs=len(seqs), kv_dtype=KV_BF16)
+    ctx = [synth.kv_normal(71, s, cfg, n) for s, n in zip(seqs, X3_LENS)]
+    for s, (k, v) in zip(seqs, ctx):
+        kv.write(s, k, v)
+    assert m.attention_kernel(kv, len(seqs)) == "paged_attention_exact3_kernel"
+    toks = synth.uniform_u32(3, 3, len(seqs), 0, cfg.vocab_size - 1).tolist()
+    for step in range(2):
+        nxt, logits = m.decode_step(kv, seqs, toks, want_logits=True)
+        for i, s in enumerate(seqs):
+            okv = om.kv(X3_LENS[i] + 4, bf16=True)
+            okv.seed(*ctx[i])
+            if step:
+                om.forward(okv, [prev[i]], X3_LENS[i])
+            r = om.forward(okv, [toks[i]], X3_LENS[i] + step)
+            np.testing.assert_array_equal(logits[i], r, err_msg=f"context {X3_LENS[i]} step {step}")
+        prev, toks = toks, [int(x) for x in nxt]
+    m.set_numerics("auto")
+
+
+def test_reference_order_prefill_bf16_hd128(cuda_backend, gqa4_2kv):
+    """A 200-token prompt in one step (every token attends causally through
+    the same kernel), then decode: bit-identical logits."""
+    cfg, w = gqa4_2kv
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=256)
+    kv = m.new_kv_cache(num_pages=32, kv_dtype=KV_BF16)
+    om = O.OracleModel(w)
+    okv = om.kv(cfg.max_position_embeddings, bf16=True)
+    toks = synth.uniform_u32(13, 5, 203, 0, cfg.vocab_size - 1).tolist()
+    assert m.attention_kernel(kv, 200) == "paged_attention_exact3_kernel"
+    np.testing.assert_array_equal(m.forward(toks[:200], 0, kv), om.forward(okv, toks[:200], 0))
+    for i in range(200, 203):
+        np.testing.assert_array_equal(m.forward([toks[i]], i, kv), om.forward(okv, [toks[i]], i))
+
+
 def test_errors(cuda_backend, small):
     from bitnetrs_b200 import BackendError, InvalidConfig, InvalidShape
 
@@ -270,7 +324,8 @@ def _raise_invalid_config(backend):
     N.check(N.cuda_lib().bitnet_cuda_model_create(backend.handle, C.byref(cfg), C.byref(wts), 8, C.byref(h)))
 
 
-def test_2b_greedy_decode_token_identical(cuda_backend):
+@pytest.mark.parametrize("kv_dtype", [KV_F32, KV_BF16], ids=["f32kv", "bf16kv"])
+def test_2b_greedy_decode_token_identical(cuda_backend, kv_dtype):
     """2B architecture, random init, 128-token seeded
     prompt, 128 greedy tokens at batch 1.  The oracle decodes greedily; the
     GPU is fed the same tokens (teacher forcing) so every step's logits are
@@ -280,9 +335,9 @@ def test_2b_greedy_decode_token_identical(cuda_backend):
     w = synth.random_model(cfg, seed=0)
     prompt = synth.uniform_u32(0, 2, 128, 0, cfg.vocab_size - 1).tolist()
     m = BitNetModel(w, cuda_backend, max_batch_tokens=256)
-    kv = m.new_kv_cache(num_pages=32)
+    kv = m.new_kv_cache(num_pages=32, kv_dtype=kv_dtype)
     om = O.OracleModel(w)
-    okv = om.kv(cfg.max_position_embeddings)
+    okv = om.kv(cfg.max_position_embeddings, bf16=(kv_dtype == KV_BF16))
     L = O.lib()
     g = m.forward(prompt, 0, kv)
     r = om.forward(okv, prompt, 0)
