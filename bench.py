@@ -47,17 +47,19 @@ def args():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller contexts keep profiler captures of the same kernels to a few GB
+    ap.add_argument("--ctx-hi", type=int, default=CTX_HI, help="largest seeded context (default C4's 4096)")
     return ap.parse_args()
 
 
-def model_config():
+def model_config(ctx_hi=CTX_HI):
     from bitnetrs_b200 import bitnet_2b_config
 
     cfg = bitnet_2b_config()
     # Contexts reach 4096 + decode steps, past the 2B model's 4096; RoPE is
     # defined for any position (the reference rebuilds its cache), so the
     # benchmark model accepts 4096 + 512 positions.
-    cfg.max_position_embeddings = CTX_HI + 512
+    cfg.max_position_embeddings = ctx_hi + 512
     return cfg
 
 
@@ -228,13 +230,13 @@ def run_cuda(a):
     from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, kernel_launches, synth
 
     B, K, W = a.batch, a.steps, a.warmup
-    cfg = model_config()
+    cfg = model_config(a.ctx_hi)
     t_setup = time.perf_counter()
     weights = synth.random_model(cfg, seed=SEED)
     backend = CudaBackend(local)
     model = BitNetModel(weights, backend, max_batch_tokens=max(B, 256))
     rank_seed = SEED + 1000 * rank
-    ctxs = synth.uniform_u32(rank_seed, 11, B, CTX_LO, CTX_HI).astype(np.int64)
+    ctxs = synth.uniform_u32(rank_seed, 11, B, CTX_LO, a.ctx_hi).astype(np.int64)
     total_steps = W + K + 3 + E2E_STEPS + 2
     pages = int(np.sum((ctxs + total_steps + 15) // 16)) + 64 + (128 + 64 + 15) // 16
     kv = model.new_kv_cache(num_pages=pages, max_seqs=B + 1, kv_dtype=KV_BF16)
@@ -372,7 +374,7 @@ def run_cuda(a):
             "data": "synthetic: random-init 2B weights N(0,0.02) absmean-ternarised; contexts U[128,4096] "
                     "seeded with N(0,1) bf16 K/V",
             "config": {"workload": "C4 continuous-batching decode, BitNet-2B shape", "batch_per_gpu": B,
-                       "global_batch": B * world, "ctx": f"U[{CTX_LO},{CTX_HI}] seeded per rank",
+                       "global_batch": B * world, "ctx": f"U[{CTX_LO},{a.ctx_hi}] seeded per rank",
                        "kv": "paged bf16, 16-token pages", "parallelism": f"dp{world} (replicated weights, no "
                                                                          f"collective)",
                        "l2": "inputs larger than L2 (~44 GB of KV read per step)"},

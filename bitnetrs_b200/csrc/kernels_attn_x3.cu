@@ -15,11 +15,12 @@
 //     tile load per page (128-byte swizzle; slot layout [16 rows][2 halves]
 //     [64 bf16], the 16-byte chunk c of 128-byte unit u = 2*row + half
 //     stored at chunk c ^ (u & 7)): first the K blocks of every page, then
-//     the V blocks.  Warp 8 issues every load (issuing a bulk copy holds the
-//     issuing thread for ~150 cycles, so it stays off the compute warps).  A
-//     slot's "full" mbarrier counts the TMA bytes; its "empty" signal is
+//     the V blocks.  Warp 8 issues the loads, kX3Batch at a time from
+//     separate lanes (issuing a bulk copy holds the issuing thread for ~150
+//     cycles, so it stays off the compute warps).
+//     A slot's "full" mbarrier counts the TMA bytes; its "empty" signal is
 //     named barrier 1 + slot: the four warps that read the slot bar.arrive,
-//     the loader bar.syncs before refilling it.
+//     the loader warp bar.syncs before refilling it.
 //   * QK: warps 4g..4g+3 take pages g, g+2, ... (4 positions each); eight
 //     lanes per position, lane (jq, hp) runs FMA chains 2jq and 2jq+1 of heads
 //     2hp and 2hp+1 (fmaf, one rounding each, as _mm256_fmadd_ps); two
@@ -43,7 +44,8 @@ namespace {
 constexpr int kX3Slots = 8;            // ring depth (pages of K or V)
 constexpr int kX3SlotBytes = 4096;     // [16 rows][2 halves][64 bf16], 128-byte swizzled
 constexpr int kX3Warps = 8;            // compute warps: QK (four per page), softmax, PV (warps 0-3)
-constexpr int kX3Threads = (kX3Warps + 1) * 32;
+constexpr int kX3Threads = (kX3Warps + 1) * 32;  // + the loader warp
+constexpr int kX3Batch = 2;            // loads the loader issues per step, one lane each
 constexpr int kX3ComputeThreads = kX3Warps * 32;
 constexpr int kX3SlotBar = 160;        // threads meeting at a slot's named barrier (4 readers + loader)
 constexpr int kX3MaxCand = 256;        // queued exp-table lookups per CTA
@@ -69,14 +71,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Waits for the phase of `parity` to complete.  Returns false when it has not
 // completed within kX3WaitCycles, or (when abort_flag is given) as soon as
 // another warp of the CTA has given up.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (abort_flag && *abort_flag) return false;
     if (clock64() - t0 > kX3WaitCycles) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag);
 }
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int y, int z, uint32_t bar) {
   asm volatile(
@@ -85,19 +89,52 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "l"((uint64_t)map), "r"(0), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
-// Byte offset of 16-byte chunk `c` (0..15) of `row` in a slot.
-__device__ __forceinline__ int slot_chunk(int row, int c) {
-  const int u = 2 * row + (c >> 3);
-  return u * 128 + (((c & 7) ^ (u & 7)) << 4);
-}
 
 // Named barriers: 0 = __syncthreads, 1..kX3Slots = slot s is free again,
 // kX3Slots + 1 = the compute warps.
+template <int ID>
+__device__ __forceinline__ void bar_arrive_id() {
+  asm volatile("bar.arrive %0, %1;\n" ::"n"(ID), "n"(kX3SlotBar) : "memory");
+}
+template <int ID>
+__device__ __forceinline__ void bar_sync_id() {
+  asm volatile("bar.sync %0, %1;\n" ::"n"(ID), "n"(kX3SlotBar) : "memory");
+}
+// Immediate barrier ids (a register id costs uniform-datapath moves per use).
 __device__ __forceinline__ void slot_release(int s) {
-  asm volatile("bar.arrive %0, %1;\n" ::"r"(1 + s), "n"(kX3SlotBar) : "memory");
+  switch (s) {
+    case 0: bar_arrive_id<1>(); break;
+    case 1: bar_arrive_id<2>(); break;
+    case 2: bar_arrive_id<3>(); break;
+    case 3: bar_arrive_id<4>(); break;
+    case 4: bar_arrive_id<5>(); break;
+    case 5: bar_arrive_id<6>(); break;
+    case 6: bar_arrive_id<7>(); break;
+    default: bar_arrive_id<8>(); break;
+  }
 }
 __device__ __forceinline__ void slot_wait_free(int s) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(1 + s), "n"(kX3SlotBar) : "memory");
+  switch (s) {
+    case 0: bar_sync_id<1>(); break;
+    case 1: bar_sync_id<2>(); break;
+    case 2: bar_sync_id<3>(); break;
+    case 3: bar_sync_id<4>(); break;
+    case 4: bar_sync_id<5>(); break;
+    case 5: bar_sync_id<6>(); break;
+    case 6: bar_sync_id<7>(); break;
+    default: bar_sync_id<8>(); break;
+  }
+}
+static_assert(kX3Slots == 8, "slot barriers are spelled out for 8 slots");
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(a));
+  return v;
 }
 __device__ __forceinline__ void compute_bar() {
   asm volatile("bar.sync %0, %1;\n" ::"n"(kX3Slots + 1), "n"(kX3ComputeThreads) : "memory");
@@ -112,7 +149,7 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kX3Slots];
   __shared__ __align__(16) float4 qs[16 * 8];  // [chunk][jq][hp]: q[2hp][8c+2jq..+1], q[2hp+1][8c+2jq..+1]
-  __shared__ int slot_issued[kX3Slots];        // loads issued into each slot
+  __shared__ int issued_sh;                    // loads issued (0 .. issued_sh-1)
   __shared__ uint2 cand[kX3MaxCand];           // (float index into the scores, exp input bits)
   __shared__ float red[kX3Warps][4];
   __shared__ float hmax[4], hinv[4];
@@ -142,7 +179,6 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
       qs[tid] = make_float4(a.x, a.y, b.x, b.y);
     }
   }
-  if (tid < kX3Slots) slot_issued[tid] = 0;
   if (tid == 0) {
     for (int s = 0; s < kX3Slots; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
     abort_flag = 0;
@@ -154,21 +190,32 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
 
   if (warp == kX3Warps) {
     // ---------------- loader: load i (K page i, or V page i - n) into slot i % kX3Slots ----------------
-    for (int i = 0; i < total; ++i) {
-      const int s = i % kX3Slots;
-      if (i >= kX3Slots) slot_wait_free(s);  // the readers of load i - kX3Slots are done
-      if (lane == 0 && !*abort_p) {
-        const int kind = i < n ? 0 : 1;
-        const uint32_t bar = smem_u32(&full_bar[s]);
-        mbar_expect_tx(bar, kX3SlotBytes);
-        tma_load_4d(smem_u32(ring + s * kX3SlotBytes), &tmap, (kvh * 2 + kind) * kPage, pages[kind ? i - n : i], bar);
-        slot_issued[s] += 1;
-      }
+    // Each step frees kX3Batch slots (named barriers) and lanes 0..kX3Batch-1 issue
+    // one load each: issuing holds a thread for ~150 cycles, and a single thread
+    // issuing page by page falls behind the QK warps.
+    auto issue = [&](int i) {
+      const int s = i % kX3Slots, kind = i < n ? 0 : 1;
+      const uint32_t bar = smem_u32(&full_bar[s]);
+      mbar_expect_tx(bar, kX3SlotBytes);
+      tma_load_4d(smem_u32(ring + s * kX3SlotBytes), &tmap, (kvh * 2 + kind) * kPage, pages[kind ? i - n : i], bar);
+    };
+    // Invariant: the readers of loads [0, i - kX3Slots) have been waited for,
+    // each exactly once (the readers arrive once per load, issued or not).
+    int i = min(total, kX3Slots), issued = i;
+    if (lane < i) issue(lane);
+    while (i < total) {
+      const int nb = min(kX3Batch, total - i);
+      for (int b = 0; b < nb; ++b) slot_wait_free((i + b) % kX3Slots);  // readers of load i+b-kX3Slots are done
+      i += nb;
+      if (*abort_p) break;
+      if (lane < nb) issue(i - nb + lane);
+      issued = i;
       __syncwarp();
     }
-    // complete the slot barriers of the last loads, so that no named barrier
-    // is left with pending arrivals
-    for (int i = max(total, kX3Slots); i < total + kX3Slots; ++i) slot_wait_free(i % kX3Slots);
+    if (lane == 0) issued_sh = issued;
+    // wait for the readers of loads [i - kX3Slots, total), so that no named
+    // barrier is left with pending arrivals
+    for (int k = max(i, kX3Slots); k < total + kX3Slots; ++k) slot_wait_free(k % kX3Slots);
   } else {
     auto wait_full = [&](int i) {
       if (!mbar_wait(smem_u32(&full_bar[i % kX3Slots]), (i / kX3Slots) & 1, abort_p) && !*abort_p) {
@@ -183,13 +230,18 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
       const int hp = (lane >> 2) & 1;   // heads 2hp, 2hp+1
       const int r = (warp & 3) * 4 + (lane >> 3);  // row (position) within the page
       const float4* qv = qs + jq * 2 + hp;
+      // chunk c of row r sits in unit u = 2r + (c >> 3) at chunk (c & 7) ^ (u & 7);
+      // the unit's base has no bits in 4..6, so the offset is base_u ^ ((c & 7) << 4)
+      const uint32_t kb0 = (uint32_t)((2 * r) * 128 + (((2 * r) & 7) << 4) + jq * 4);
+      const uint32_t kb1 = (uint32_t)((2 * r + 1) * 128 + (((2 * r + 1) & 7) << 4) + jq * 4);
+      const uint32_t ring_s = smem_u32(ring);
       for (int P = warp >> 2; P < n; P += 2) {
         wait_full(P);
         const int s = P % kX3Slots;
-        const uint8_t* kb = ring + s * kX3SlotBytes + jq * 4;
+        const uint32_t ka0 = ring_s + s * kX3SlotBytes + kb0, ka1 = ring_s + s * kX3SlotBytes + kb1;
         uint32_t w[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) w[c] = *reinterpret_cast<const uint32_t*>(kb + slot_chunk(r, c));
+        for (int c = 0; c < 16; ++c) w[c] = lds_u32((c < 8 ? ka0 : ka1) ^ ((c & 7) << 4));
         slot_release(s);
         // chains 2jq, 2jq+1 of head 2hp (a0, a1) and of head 2hp+1 (b0, b1)
         float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
@@ -307,21 +359,41 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
     // ---------------- PV (warps 0-3) ----------------
     if (warp < 4) {
       const int d = 32 * warp + lane;                        // dim of this lane, all four heads
-      const int vbyte = (d & 7) * 2, vchunk = d >> 3;
+      // row rr of the lane's dim: unit u = 2rr + h (h = d >> 6), chunk ((d >> 3) & 7) ^ (u & 7),
+      // byte 2 (d & 7); the swizzle repeats every 4 rows: offset = 256 rr + vo[rr & 3]
+      // with vo[k] the offset of row k less 256 k
+      uint32_t vo[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int u = 2 * k + (d >> 6);  // unit of row k; row rr = k + 4m sits 1024 m (= 256 (rr - k)) further
+        vo[k] = (uint32_t)((d >> 6) * 128 + ((((d >> 3) & 7) ^ (u & 7)) << 4) + (d & 7) * 2);
+      }
+      const uint32_t ring_s = smem_u32(ring);
       float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
       for (int P = 0; P < n; ++P) {
         const int i = n + P, s = i % kX3Slots;
         wait_full(i);
-        const uint8_t* vb = ring + s * kX3SlotBytes + vbyte;
+        const uint32_t sb = ring_s + s * kX3SlotBytes;
         const int rows = min(kPage, ctx - P * kPage);
         const float4* pp = sc + P * kPage;
         uint32_t v[kPage];
 #pragma unroll
-        for (int rr = 0; rr < kPage; ++rr) v[rr] = *reinterpret_cast<const uint16_t*>(vb + slot_chunk(rr, vchunk));
+        for (int rr = 0; rr < kPage; ++rr) v[rr] = lds_u16(sb + vo[rr & 3] + 256 * rr);
         slot_release(s);
+        if (rows == kPage) {
 #pragma unroll
-        for (int rr = 0; rr < kPage; ++rr) {
-          if (rr < rows) {
+          for (int rr = 0; rr < kPage; ++rr) {
+            const float4 p = pp[rr];
+            const float x = __uint_as_float(v[rr] << 16);
+            o0 = __fmaf_rn(p.x, x, o0);
+            o1 = __fmaf_rn(p.y, x, o1);
+            o2 = __fmaf_rn(p.z, x, o2);
+            o3 = __fmaf_rn(p.w, x, o3);
+          }
+        } else {
+#pragma unroll
+          for (int rr = 0; rr < kPage; ++rr) {
+            if (rr >= rows) break;
             const float4 p = pp[rr];
             const float x = __uint_as_float(v[rr] << 16);
             o0 = __fmaf_rn(p.x, x, o0);
@@ -342,8 +414,8 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
   // After a failed wait, loads may still be landing in the ring: wait (again
   // bounded) for the last load issued into each slot before the CTA exits.
   if (abort_flag && tid == 0)
-    for (int s = 0; s < kX3Slots; ++s)
-      if (slot_issued[s] > 0) mbar_wait(smem_u32(&full_bar[s]), (slot_issued[s] - 1) & 1, nullptr);
+    for (int k = max(0, issued_sh - kX3Slots); k < issued_sh; ++k)
+      mbar_wait(smem_u32(&full_bar[k % kX3Slots]), (k / kX3Slots) & 1, nullptr);
 }
 
 }  // namespace bitnet
