@@ -47,6 +47,7 @@ def args():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv-sweep", action="store_true")
     # smaller contexts keep profiler captures of the same kernels to a few GB
     ap.add_argument("--ctx-hi", type=int, default=CTX_HI, help="largest seeded context (default C4's 4096)")
     return ap.parse_args()
@@ -119,6 +120,82 @@ class Clocks:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Decode GEMV (M = 1) over the 2B layer shapes
+# ---------------------------------------------------------------------------
+GEMV_SHAPES = [("qkv", 3840, 2560), ("o", 2560, 2560), ("gate_up", 13824, 2560), ("down", 2560, 6912)]
+
+
+def gemv_sweep(backend, dev, peak_gbs, min_bytes=320e6):
+    """Back-to-back M=1 ternary GEMVs of each fused 2B projection, captured in
+    a CUDA graph; the graph cycles through enough weight copies (> 2x L2) that
+    every launch streams its weights from HBM.  Algorithmic bytes per launch:
+    N*K/4 packed weights + K int8 activations + 4 (absmax) + 4N f32 outputs."""
+    import ctypes as C
+
+    import torch
+
+    from bitnetrs_b200 import _native as N
+    from bitnetrs_b200 import synth
+
+    lib = N.cuda_lib()
+    out = {}
+    tot_b, tot_ms = 0.0, 0.0
+    for name, n, k in GEMV_SHAPES:
+        packed = synth.ternary_codes(SEED, 17, n, k)
+        wbytes = n * k / 4
+        copies = max(2, int(np.ceil(min_bytes / wbytes)))
+        handles = []
+        for _ in range(copies):
+            h = C.c_void_p()
+            N.check(lib.bitnet_cuda_weight_upload(backend.handle, packed.ctypes.data, packed.size, n, k, 0.02,
+                                                  C.byref(h)))
+            handles.append(h)
+        ldq = (k + 63) // 64 * 64
+        xb = synth.bf16_normal(SEED, 18, k, 1.0)
+        d_x = torch.from_numpy(xb.view(np.int16).copy()).to(dev)
+        d_xq = torch.zeros(ldq, dtype=torch.int8, device=dev)
+        d_amax = torch.zeros(1, dtype=torch.float32, device=dev)
+        d_rs = torch.zeros(1, dtype=torch.int32, device=dev)
+        d_st = torch.zeros(1, dtype=torch.int32, device=dev)
+        d_out = torch.zeros(n, dtype=torch.float32, device=dev)
+        s = torch.cuda.Stream(device=dev)
+        torch.cuda.synchronize()
+        N.check(lib.bitnet_cuda_quantize_rows_device(backend.handle, d_x.data_ptr(), 1, 1, k, d_xq.data_ptr(), ldq,
+                                                     d_amax.data_ptr(), d_rs.data_ptr(), d_st.data_ptr(),
+                                                     C.c_void_p(s.cuda_stream)))
+        torch.cuda.synchronize()
+        reps = 2 * copies
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                N.check(lib.bitnet_cuda_ternary_matmul_device(backend.handle, handles[i % copies], d_xq.data_ptr(),
+                                                              ldq, d_amax.data_ptr(), d_rs.data_ptr(), 1,
+                                                              d_out.data_ptr(), None, C.c_void_p(s.cuda_stream)))
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(3):
+                g.replay()
+            e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (3 * reps)
+        b = wbytes + k + 4 + 4 * n
+        out[name] = {"N": n, "K": k, "us_per_launch": round(ms * 1e3, 3), "gbs": round(b / (ms / 1e3) / 1e9, 1),
+                     "frac": round(b / (ms / 1e3) / 1e9 / peak_gbs, 3)}
+        tot_b += b
+        tot_ms += ms
+        del g
+        for h in handles:
+            lib.bitnet_cuda_weight_destroy(h)
+    out["per_layer"] = {"us": round(tot_ms * 1e3, 3), "gbs": round(tot_b / (tot_ms / 1e3) / 1e9, 1),
+                        "frac": round(tot_b / (tot_ms / 1e3) / 1e9 / peak_gbs, 3)}
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -357,6 +434,11 @@ def run_cuda(a):
           "kernels_ms_per_token": {k: round(v[0], 4) for k, v in kt1.items()}}
     model.check()
 
+    # ---- decode GEMV sweep (rank 0) ----
+    gemv_m1 = None
+    if rank == 0 and not a.no_gemv_sweep:
+        gemv_m1 = gemv_sweep(backend, dev, peak)
+
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -385,6 +467,7 @@ def run_cuda(a):
                          "traffic": traffic_from_profiles(attn_kernel),
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": attn_bytes,
                          "avg_launch_ms": attn_launch_ms},
+            "gemv_m1": gemv_m1,
             "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32, mma.sync)", "ms_per_step": mm_ms,
                      "launches": mm_n, "hbm_gbs": (w_bytes + act_bytes) / (mm_ms / 1e3) / 1e9 if mm_ms else None,
                      "tops": mm_ops / (mm_ms / 1e3) / 1e12 if mm_ms else None},

@@ -270,6 +270,8 @@ int stage_xq(bitnet_cuda_ctx* c, const int8_t* xq, size_t K) {
 // Quantise host f32 x (length K) on the device into b2 (padded) and b3
 // (act_absmax); returns QuantizationError on a non-finite input.
 int device_quantize(bitnet_cuda_ctx* c, const float* x, size_t K, float* scale_out) {
+  if (K > (size_t)kMaxRowFloats)
+    return backend_error("activation rows longer than " + std::to_string(kMaxRowFloats) + " are not supported");
   cudaStream_t st = c->stream;
   BN_TRY(upload(c->b[6], x, K * sizeof(float), st));
   BN_TRY(c->b[2].ensure(padded_cols(K)));
@@ -321,6 +323,10 @@ int bitnet_cuda_create(uint32_t device_id, bitnet_cuda_ctx** out) {
   if (rc) {
     delete c;
     return rc;
+  }
+  if (row_kernels_prepare() != 0) {
+    delete c;
+    return backend_error("raising the shared-memory limit of the row kernels failed");
   }
   *out = c;
   return BITNET_OK;
@@ -407,6 +413,8 @@ int bitnet_cuda_rms_norm(bitnet_cuda_ctx* c, const float* x, size_t xl, const fl
   if (xl != ol) return shape_error("input.len() == output.len() = " + sz(xl), "output.len() = " + sz(ol));
   if (!(eps > 0.0f) || !std::isfinite(eps)) return quant_error("eps must be finite and > 0");
   if (xl == 0) return BITNET_OK;
+  if (xl > (size_t)kMaxRowFloats)
+    return backend_error("rms_norm rows longer than " + sz(kMaxRowFloats) + " are not supported");
   Guard g(c);
   cudaStream_t st = c->stream;
   BN_TRY(upload(c->b[0], x, xl * 4, st));
@@ -637,6 +645,7 @@ int bitnet_cuda_quantize_rows_device(bitnet_cuda_ctx* c, const void* x, int x_is
                                      size_t ldq, float* act_absmax, int32_t* row_sum, int32_t* status, void* stream) {
   if (K == 0) return quant_error("cannot quantise an empty activation vector");
   if (ldq < K || ldq % 64 != 0) return shape_error("ldq >= K and a multiple of 64", "ldq = " + sz(ldq));
+  if (K > (size_t)kMaxRowFloats) return shape_error("K <= " + sz(kMaxRowFloats), "K = " + sz(K));
   cudaSetDevice(c->device);
   cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
   launch_quantize_rows(x, x_is_bf16 != 0, (int)K, (int)M, (int)K, xq, (int)ldq, act_absmax, nullptr, row_sum, status,

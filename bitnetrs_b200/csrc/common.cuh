@@ -180,6 +180,16 @@ __device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
   return exp_table_lookup(__float_as_uint(x), f, t);
 }
 
+// Programmatic dependent launch (griddepcontrol, sm_90+).  A kernel launched
+// with launch_pdl may begin while the previous kernel in the stream is still
+// running; it must call pdl_wait() before it reads anything an earlier kernel
+// writes or writes anything an earlier kernel reads (pdl_wait returns once
+// the previous grid has completed and its memory is visible).  Only loads of
+// data no kernel writes (weights) may precede it.  pdl_launch_dependents()
+// allows the next kernel to start its own prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 // Rust f32::round: half away from zero (roundf), then clamp, then cast.
 __device__ __forceinline__ int8_t quant_i8(float x, float inv) {
   float s = roundf(__fmul_rn(x, inv));

@@ -13,6 +13,23 @@ constexpr int kStatusBadToken = 2;     // token id >= vocab_size
 constexpr int kStatusBadContext = 4;   // a token's context exceeds the kernel's capacity
 constexpr int kStatusWaitTimeout = 8;  // a bounded device-side wait gave up
 
+// Launch with programmatic stream serialisation (the kernel must follow the
+// pdl_wait rule of common.cuh).
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Per-launch kernel counter (reported by bitnet_cuda_kernel_launches).
 void count_launch(uint64_t n = 1);
 void uncount_launch(uint64_t n);
@@ -28,6 +45,12 @@ void launch_repack_ternary(const uint8_t* src, uint32_t* dst, int rows, int cols
 // (either may be null); row_sum[m] = sum of xq; status |= 1 on non-finite input.
 void launch_quantize_rows(const void* x, bool x_bf16, int ldx, int M, int K, int8_t* xq, int ldq, float* act_absmax,
                           float* scale, int32_t* row_sum, int32_t* status, cudaStream_t st);
+
+// The row kernels below stage one row of up to kMaxRowFloats f32 in shared
+// memory; row_kernels_prepare raises their limit above the 48 KiB default on
+// the current device (call outside graph capture; 0 on success).
+constexpr int kMaxRowFloats = 56 * 1024;
+int row_kernels_prepare();
 
 // rms_norm in the reference order (norm.rs:113-137): out[m] = (x*inv)*w.
 void launch_rms_norm(const float* x, int ldx, const float* w, int d, float eps, float* out, int ldo, int M,

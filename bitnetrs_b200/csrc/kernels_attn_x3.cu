@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
   __shared__ int abort_flag, ncand;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x, kvh = blockIdx.y;
+  pdl_launch_dependents();
+  pdl_wait();
   const int ctx = tok_pos[t] + 1;
   if (ctx > cap || ctx <= 0) {  // uniform over the block
     if (tid == 0) atomicOr(status, kStatusBadContext);
@@ -381,14 +383,26 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
         for (int rr = 0; rr < kPage; ++rr) v[rr] = lds_u16(sb + vo[rr & 3] + 256 * rr);
         slot_release(s);
         if (rows == kPage) {
+          // p of the next four rows is loaded while the current four are used
+          float4 pa[4], pb[4];
 #pragma unroll
-          for (int rr = 0; rr < kPage; ++rr) {
-            const float4 p = pp[rr];
-            const float x = __uint_as_float(v[rr] << 16);
-            o0 = __fmaf_rn(p.x, x, o0);
-            o1 = __fmaf_rn(p.y, x, o1);
-            o2 = __fmaf_rn(p.z, x, o2);
-            o3 = __fmaf_rn(p.w, x, o3);
+          for (int k = 0; k < 4; ++k) pa[k] = pp[k];
+#pragma unroll
+          for (int g4 = 0; g4 < 4; ++g4) {
+            if (g4 < 3) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) pb[k] = pp[4 * (g4 + 1) + k];
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float x = __uint_as_float(v[4 * g4 + k] << 16);
+              o0 = __fmaf_rn(pa[k].x, x, o0);
+              o1 = __fmaf_rn(pa[k].y, x, o1);
+              o2 = __fmaf_rn(pa[k].z, x, o2);
+              o3 = __fmaf_rn(pa[k].w, x, o3);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) pa[k] = pb[k];
           }
         } else {
 #pragma unroll
@@ -477,8 +491,8 @@ void launch_paged_attention_exact3(const float* q, int T, int nh, const int32_t*
                                    const int32_t* page_table, const KvGeom& kv, const CUtensorMap& map, int layer,
                                    int max_ctx, float* out, const ExpTable& et, int32_t* status, cudaStream_t st) {
   if (T <= 0) return;
-  paged_attention_exact3_kernel<<<dim3(T, kv.kv_heads), kX3Threads, exact3_smem(max_ctx), st>>>(
-      q, nh, tok_pos, tok_seq, page_table, kv, layer, exact3_cap(max_ctx), out, et, status, map);
+  launch_pdl(paged_attention_exact3_kernel, dim3(T, kv.kv_heads), dim3(kX3Threads), exact3_smem(max_ctx), st, q, nh,
+             tok_pos, tok_seq, page_table, kv, layer, exact3_cap(max_ctx), out, et, status, map);
   count_launch();
 }
 

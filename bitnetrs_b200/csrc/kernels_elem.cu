@@ -173,6 +173,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   __shared__ float bc;
   __shared__ float red_f[32];
   __shared__ int red_i[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.x;
   const float* xr = x + (size_t)m * ldx;
   const bool vec = (d & 3) == 0 && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0 && (!GATE_UP || ((uintptr_t)x2 & 15) == 0);
@@ -206,14 +208,27 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   quantize_row_smem(row, d, xq + (size_t)m * ldq, ldq, act_absmax + m, nullptr, row_sum + m, status, red_f, red_i);
 }
 
+int row_kernels_prepare() {
+  const int bytes = kMaxRowFloats * (int)sizeof(float);
+  int bad = 0;
+  bad |= cudaFuncSetAttribute(quantize_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(quantize_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
+  return bad;
+}
+
 void launch_norm_quant(const float* x, const float* x2, int ldx, const float* w, int d, float eps, int8_t* xq, int ldq,
                        float* act_absmax, int32_t* row_sum, int32_t* status, int M, cudaStream_t st) {
   if (M <= 0) return;
   size_t smem = (size_t)d * sizeof(float);
   if (x2)
-    norm_quant_kernel<true><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
+    launch_pdl(norm_quant_kernel<true>, dim3(M), dim3(256), smem, st, x, x2, ldx, w, d, eps, xq, ldq, act_absmax,
+               row_sum, status);
   else
-    norm_quant_kernel<false><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
+    launch_pdl(norm_quant_kernel<false>, dim3(M), dim3(256), smem, st, x, x2, ldx, w, d, eps, xq, ldq, act_absmax,
+               row_sum, status);
   count_launch();
 }
 

@@ -58,11 +58,93 @@ __device__ __forceinline__ void epilogue_store(float* out, int ldo, int m, int n
 }
 
 // ---------------------------------------------------------------------------
-// M = 1 GEMV: each warp streams R consecutive rows as one contiguous run of
-// 16-byte chunks (perfectly coalesced), x lives in shared memory.
+// M = 1 GEMV (decode).  A warp owns R consecutive rows.  Every lane first
+// issues its 16-byte streaming loads of those rows (chunk lane + 32 j of each
+// row, j < CH), then the block stages x in shared memory and sums it while
+// the weight loads are in flight, then each lane multiplies its codes by x
+// with dp4a and the warp reduces.  One DRAM round trip per block, every load
+// 128-bit and coalesced.
 // ---------------------------------------------------------------------------
+template <int R, int CH>
+__global__ void __launch_bounds__(256) gemv_m1_kernel(const uint32_t* __restrict__ W, int N, int kw,
+                                                      const int8_t* __restrict__ xq, const float* __restrict__ amax,
+                                                      Segments seg, Epi epi, float* __restrict__ out,
+                                                      int32_t* __restrict__ acc_out) {
+  extern __shared__ uint4 xs4[];  // kw*16 bytes of x
+  __shared__ int red[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kw4 = kw >> 2;  // 16-byte chunks per row
+  const int row0 = (blockIdx.x * 8 + warp) * R;
+  const uint4* W4 = reinterpret_cast<const uint4*>(W);
+  pdl_launch_dependents();
+  uint4 w[R][CH];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const int c = lane + 32 * j;
+      w[r][j] = (row0 + r < N && c < kw4) ? __ldcs(W4 + (size_t)(row0 + r) * kw4 + c) : make_uint4(0, 0, 0, 0);
+    }
+  pdl_wait();  // weights are constant; x and out belong to the previous kernels
+  int xsum = 0;
+  const uint4* xg = reinterpret_cast<const uint4*>(xq);
+  for (int i = threadIdx.x; i < kw; i += 256) {
+    const uint4 v = xg[i];
+    xs4[i] = v;
+    xsum = __dp4a((int)v.x, 0x01010101, xsum);
+    xsum = __dp4a((int)v.y, 0x01010101, xsum);
+    xsum = __dp4a((int)v.z, 0x01010101, xsum);
+    xsum = __dp4a((int)v.w, 0x01010101, xsum);
+  }
+  xsum = warp_sum_i(xsum);
+  if (lane == 0) red[warp] = xsum;
+  __syncthreads();
+  xsum = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) xsum += red[k];
+  if (row0 >= N) return;
+  int acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const int c = lane + 32 * j;
+    if (c < kw4) {
+      const uint4* x = xs4 + 4 * c;
+      const uint4 x0 = x[0], x1 = x[1], x2 = x[2], x3 = x[3];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t wv[4] = {w[r][j].x, w[r][j].y, w[r][j].z, w[r][j].w};
+        const uint4 xv[4] = {x0, x1, x2, x3};
+        int d = acc[r];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          d = __dp4a((int)(wv[q] & 0x03030303u), (int)xv[q].x, d);
+          d = __dp4a((int)((wv[q] >> 2) & 0x03030303u), (int)xv[q].y, d);
+          d = __dp4a((int)((wv[q] >> 4) & 0x03030303u), (int)xv[q].z, d);
+          d = __dp4a((int)((wv[q] >> 6) & 0x03030303u), (int)xv[q].w, d);
+        }
+        acc[r] = d;
+      }
+    }
+  }
+  const float am = amax[0];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int s = warp_sum_i(acc[r]);
+    if (lane == 0 && row0 + r < N) {
+      const int n = row0 + r;
+      const int32_t a = xsum - s;
+      if (acc_out) acc_out[n] = a;
+      epilogue_store(out, 0, 0, n, dequant(a, seg_scale(seg, n), am), epi);
+    }
+  }
+}
+
+// M = 1 for rows longer than 8192 codes: each warp streams R rows as one
+// run of 16-byte chunks.
 template <int R>
-__global__ void __launch_bounds__(128) gemv_m1_kernel(const uint32_t* __restrict__ W, int N, int kw,
+__global__ void __launch_bounds__(128) gemv_m1_long_kernel(const uint32_t* __restrict__ W, int N, int kw,
                                                       const int8_t* __restrict__ xq, const float* __restrict__ amax,
                                                       Segments seg, Epi epi, float* __restrict__ out,
                                                       int32_t* __restrict__ acc_out) {
@@ -142,6 +224,8 @@ __global__ void __launch_bounds__(WARPS_M* WARPS_N * 32)
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* xs = smem;
   uint8_t* wsm = smem + STAGES * BM * XS;
+  pdl_launch_dependents();
+  pdl_wait();
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wm = warp / WARPS_N, wn = warp % WARPS_N;
@@ -240,8 +324,8 @@ static void run_mma(const uint32_t* W, int N, int kw, const int8_t* xq, int ldq,
   constexpr int smem = 3 * (BM * (128 + 16) + BN * 48);
   static_assert(smem <= 48 * 1024, "dynamic shared memory above the default limit");
   dim3 grid((unsigned)ceil_div(N, BN), (unsigned)ceil_div(M, BM));
-  ternary_mma_kernel<BM, BN, WM, WN><<<grid, WM * WN * 32, smem, st>>>(W, N, kw, xq, ldq, M, amax, rowsum, seg, epi,
-                                                                      out, ldo, acc);
+  launch_pdl(ternary_mma_kernel<BM, BN, WM, WN>, grid, dim3(WM * WN * 32), smem, st, W, N, kw, xq, ldq, M, amax, rowsum,
+             seg, epi, out, ldo, acc);
   count_launch();
 }
 
@@ -251,10 +335,39 @@ void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, in
   const int kw = (int)words_per_row(K);
   if (M <= 0 || N <= 0) return;
   if (M == 1) {
-    constexpr int R = 2;
-    int rows_per_block = 4 * R;
-    gemv_m1_kernel<R><<<(unsigned)ceil_div(N, rows_per_block), 128, (size_t)kw * 16, st>>>(
-        W, N, kw, xq, act_absmax, seg, epi, out, acc);
+    const int kw4 = kw / 4;
+    const size_t smem = (size_t)kw * 16;
+    if (kw4 > 32 * 8 || smem > 48 * 1024) {
+      constexpr int R = 2;
+      gemv_m1_long_kernel<R><<<(unsigned)ceil_div(N, 4 * R), 128, smem, st>>>(W, N, kw, xq, act_absmax, seg, epi,
+                                                                              out, acc);
+      count_launch();
+      return;
+    }
+    // rows per warp: keep at least ~2 blocks of 8 warps per SM
+    const int R = N >= 9472 ? 4 : (N >= 4736 ? 2 : 1);
+    const unsigned grid = (unsigned)ceil_div(N, 8 * R);
+#define BN_GEMV(RR, CC) \
+  launch_pdl(gemv_m1_kernel<RR, CC>, dim3(grid), dim3(256), smem, st, W, N, kw, xq, act_absmax, seg, epi, out, acc)
+#define BN_GEMV_R(CC) \
+  do {                \
+    if (R == 4)       \
+      BN_GEMV(4, CC); \
+    else if (R == 2)  \
+      BN_GEMV(2, CC); \
+    else              \
+      BN_GEMV(1, CC); \
+  } while (0)
+    if (kw4 <= 32)
+      BN_GEMV_R(1);
+    else if (kw4 <= 64)
+      BN_GEMV_R(2);
+    else if (kw4 <= 128)
+      BN_GEMV_R(4);
+    else
+      BN_GEMV_R(8);
+#undef BN_GEMV_R
+#undef BN_GEMV
     count_launch();
     return;
   }

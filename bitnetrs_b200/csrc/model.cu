@@ -119,6 +119,9 @@ int validate_config(const bitnet_cuda_config& c) {
   if (c.num_hidden_layers == 0) return config_error("num_hidden_layers must be > 0");
   if (c.intermediate_size == 0) return config_error("intermediate_size must be > 0");
   if (c.max_position_embeddings == 0) return config_error("max_position_embeddings must be > 0");
+  if (c.hidden_size > (uint32_t)kMaxRowFloats || c.intermediate_size > (uint32_t)kMaxRowFloats)
+    return config_error("hidden_size and intermediate_size must be <= " + sz(kMaxRowFloats) +
+                        " (rows staged in shared memory)");
   if (!(c.rope_theta > 0.0f)) return config_error("rope_theta must be > 0");
   if (!(c.rms_norm_eps > 0.0f)) return config_error("rms_norm_eps must be > 0");
   return BITNET_OK;

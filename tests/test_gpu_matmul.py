@@ -75,3 +75,41 @@ def test_device_matmul_bit_exact(cuda_backend, M, N_, K):
         assert L.orc_ternary_gemv_preq(O.p(packed), packed.size, scale, O.p(np.ascontiguousarray(xq[m])), K,
                                        float(amax[m]), O.p(ro), N_, N_, K, None) == 0
         np.testing.assert_array_equal(out[m], ro)
+
+
+@pytest.mark.parametrize("N_,K", [(3840, 2560), (13824, 2560), (2560, 6912), (4096, 14336), (96, 20480), (33, 64)])
+def test_decode_gemv_bit_exact(cuda_backend, N_, K):
+    """M = 1 (decode) at the fused 2B shapes (qkv, gate|up), the 2B and
+    scaled-model down projections and rows past the shared-memory x stage."""
+    import torch
+
+    lib = N.cuda_lib()
+    dev = torch.device("cuda", cuda_backend.device_id)
+    packed = synth.ternary_codes(N_ + K, 5, N_, K)
+    scale = 0.0123
+    wh = C.c_void_p()
+    N.check(lib.bitnet_cuda_weight_upload(cuda_backend.handle, packed.ctypes.data, packed.size, N_, K, scale,
+                                          C.byref(wh)))
+    ldq = (K + 63) // 64 * 64
+    x_bf16 = synth.bf16_normal(K, 9, K, 1.0)
+    d_x = torch.from_numpy(x_bf16.view(np.int16).copy()).to(dev)
+    d_xq = torch.zeros((1, ldq), dtype=torch.int8, device=dev)
+    d_amax = torch.zeros(1, dtype=torch.float32, device=dev)
+    d_rs = torch.zeros(1, dtype=torch.int32, device=dev)
+    d_st = torch.zeros(1, dtype=torch.int32, device=dev)
+    d_out = torch.zeros((1, N_), dtype=torch.float32, device=dev)
+    d_acc = torch.zeros((1, N_), dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    N.check(lib.bitnet_cuda_quantize_rows_device(cuda_backend.handle, d_x.data_ptr(), 1, 1, K, d_xq.data_ptr(), ldq,
+                                                 d_amax.data_ptr(), d_rs.data_ptr(), d_st.data_ptr(), None))
+    N.check(lib.bitnet_cuda_ternary_matmul_device(cuda_backend.handle, wh, d_xq.data_ptr(), ldq, d_amax.data_ptr(),
+                                                  d_rs.data_ptr(), 1, d_out.data_ptr(), d_acc.data_ptr(), None))
+    torch.cuda.synchronize()
+    lib.bitnet_cuda_weight_destroy(wh)
+    xq = d_xq.cpu().numpy()[:, :K]
+    W = unpack_codes(packed, N_, K)
+    np.testing.assert_array_equal(d_acc.cpu().numpy(), (xq.astype(np.float64) @ W.T).astype(np.int64))
+    ro = np.zeros(N_, dtype=np.float32)
+    assert L.orc_ternary_gemv_preq(O.p(packed), packed.size, scale, O.p(np.ascontiguousarray(xq[0])), K,
+                                   float(d_amax.item()), O.p(ro), N_, N_, K, None) == 0
+    np.testing.assert_array_equal(d_out.cpu().numpy()[0], ro)
