@@ -106,6 +106,7 @@ _CUDA_SIGS = {
     "bitnet_cuda_prefill": (i32, [vp, vp, sz, vp, vp, vp, vp, vp]),
     "bitnet_cuda_generate": (i32, [vp, vp, u32, vp, sz, sz, u32, u32, vp, C.POINTER(sz)]),
     "bitnet_cuda_model_check": (i32, [vp]),
+    "bitnet_cuda_ternary_gemv_quant_noalloc": (i32, [vp, vp, vp, sz, vp, sz, vp]),
     "bitnet_cuda_model_attention_kernel": (i32, [vp, vp, u32, vp, sz]),
     "bitnet_cuda_model_set_numerics": (i32, [vp, i32]),
     "bitnet_cuda_model_set_kernel_timing": (i32, [vp, i32]),

@@ -184,6 +184,25 @@ int bitnet_cuda_ternary_matmul_device(bitnet_cuda_ctx* ctx, const bitnet_cuda_we
                                       size_t ldq, const float* act_absmax, const int32_t* row_sum, size_t M,
                                       float* out, int32_t* acc, void* stream);
 
+/* Decode GEMV with activation quantisation that allocates nothing (no
+ * counterpart in the reference): out = ternary_gemv_with_activation_quant of
+ * the uploaded weight `w` applied to x, with x (f32, x_len = in_features)
+ * and out (f32, out_len = out_features) in device memory.  For callers that
+ * must not allocate device memory on their serving path (a cudaMalloc
+ * synchronises the device and is not allowed in some host frameworks after
+ * warm-up): the activation scratch (int8 row, absmax, code sum, non-finite
+ * flag) is a fixed 32 KiB + 256 B array inside this library, so
+ * in_features is limited to 32768; longer rows return InvalidShape.  The
+ * call resets the scratch's flag itself; nothing has to start at zero.
+ *  - The first call on a device resolves the scratch's address; make it
+ *    before any stream capture on that device.
+ *  - All calls on one device share the scratch: calls that overlap in time
+ *    (other threads, or other streams still running) race; serialise them.
+ *  - Runs on `stream` (NULL = the context's stream) and returns after the
+ *    result is in `out`; a non-finite x returns QuantizationError. */
+int bitnet_cuda_ternary_gemv_quant_noalloc(bitnet_cuda_ctx* ctx, const bitnet_cuda_weight* w, const float* x,
+                                           size_t x_len, float* out, size_t out_len, void* stream);
+
 /* ===================================================================== */
 /* Device-resident model, paged KV cache, forward / decode / generate     */
 /* ===================================================================== */
