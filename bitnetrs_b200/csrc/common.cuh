@@ -186,7 +186,11 @@ __device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
 // writes or writes anything an earlier kernel reads (pdl_wait returns once
 // the previous grid has completed and its memory is visible).  Only loads of
 // data no kernel writes (weights) may precede it.  pdl_launch_dependents()
-// allows the next kernel to start its own prologue.
+// allows the next kernel to start its own prologue.  Both are no-ops for a
+// kernel launched without the attribute.  Measured on the 2B decode step,
+// only the M = 1 GEMV gains from being launched this way (its weight stream
+// starts under the previous kernel); the decode-chain kernels before it call
+// pdl_launch_dependents so that it can.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 

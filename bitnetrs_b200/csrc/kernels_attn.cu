@@ -139,8 +139,8 @@ void launch_rope_kv_store(const float* qkv, int ldqkv, int T, int nh, int nkv, i
                           const float* rope_sin, const int32_t* tok_pos, const int32_t* tok_seq,
                           const int32_t* page_table, const KvGeom& kv, int layer, float* q_out, cudaStream_t st) {
   if (T <= 0) return;
-  launch_pdl(rope_kv_store_kernel, dim3(T), dim3(256), 0, st, qkv, ldqkv, nh, nkv, hd, rope_cos, rope_sin, tok_pos,
-             tok_seq, page_table, kv, layer, q_out);
+  rope_kv_store_kernel<<<T, 256, 0, st>>>(qkv, ldqkv, nh, nkv, hd, rope_cos, rope_sin, tok_pos, tok_seq, page_table,
+                                          kv, layer, q_out);
   count_launch();
 }
 

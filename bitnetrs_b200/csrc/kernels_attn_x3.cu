@@ -491,8 +491,8 @@ void launch_paged_attention_exact3(const float* q, int T, int nh, const int32_t*
                                    const int32_t* page_table, const KvGeom& kv, const CUtensorMap& map, int layer,
                                    int max_ctx, float* out, const ExpTable& et, int32_t* status, cudaStream_t st) {
   if (T <= 0) return;
-  launch_pdl(paged_attention_exact3_kernel, dim3(T, kv.kv_heads), dim3(kX3Threads), exact3_smem(max_ctx), st, q, nh,
-             tok_pos, tok_seq, page_table, kv, layer, exact3_cap(max_ctx), out, et, status, map);
+  paged_attention_exact3_kernel<<<dim3(T, kv.kv_heads), kX3Threads, exact3_smem(max_ctx), st>>>(
+      q, nh, tok_pos, tok_seq, page_table, kv, layer, exact3_cap(max_ctx), out, et, status, map);
   count_launch();
 }
 

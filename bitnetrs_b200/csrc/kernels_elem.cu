@@ -224,11 +224,9 @@ void launch_norm_quant(const float* x, const float* x2, int ldx, const float* w,
   if (M <= 0) return;
   size_t smem = (size_t)d * sizeof(float);
   if (x2)
-    launch_pdl(norm_quant_kernel<true>, dim3(M), dim3(256), smem, st, x, x2, ldx, w, d, eps, xq, ldq, act_absmax,
-               row_sum, status);
+    norm_quant_kernel<true><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
   else
-    launch_pdl(norm_quant_kernel<false>, dim3(M), dim3(256), smem, st, x, x2, ldx, w, d, eps, xq, ldq, act_absmax,
-               row_sum, status);
+    norm_quant_kernel<false><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
   count_launch();
 }
 

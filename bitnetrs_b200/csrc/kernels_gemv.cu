@@ -324,8 +324,8 @@ static void run_mma(const uint32_t* W, int N, int kw, const int8_t* xq, int ldq,
   constexpr int smem = 3 * (BM * (128 + 16) + BN * 48);
   static_assert(smem <= 48 * 1024, "dynamic shared memory above the default limit");
   dim3 grid((unsigned)ceil_div(N, BN), (unsigned)ceil_div(M, BM));
-  launch_pdl(ternary_mma_kernel<BM, BN, WM, WN>, grid, dim3(WM * WN * 32), smem, st, W, N, kw, xq, ldq, M, amax, rowsum,
-             seg, epi, out, ldo, acc);
+  ternary_mma_kernel<BM, BN, WM, WN><<<grid, WM * WN * 32, smem, st>>>(W, N, kw, xq, ldq, M, amax, rowsum, seg, epi,
+                                                                      out, ldo, acc);
   count_launch();
 }
 
