@@ -328,6 +328,13 @@ int bitnet_cuda_create(uint32_t device_id, bitnet_cuda_ctx** out) {
     delete c;
     return backend_error("raising the shared-memory limit of the row kernels failed");
   }
+  {
+    static std::mutex tc_mu;
+    static bool tc_failed = false;
+    std::lock_guard<std::mutex> lk(tc_mu);
+    if (ternary_tc_prepare() != 0) tc_failed = true;
+    set_ternary_tc_ready(!tc_failed);
+  }
   *out = c;
   return BITNET_OK;
 }
@@ -665,7 +672,7 @@ int bitnet_cuda_ternary_matmul_device(bitnet_cuda_ctx* c, const bitnet_cuda_weig
   seg.end[0] = seg.end[1] = seg.end[2] = w->rows;
   seg.scale[0] = seg.scale[1] = seg.scale[2] = w->scale;
   launch_ternary_matmul(w->words, w->rows, w->cols, xq, (int)ldq, act_absmax, row_sum, (int)M, seg, Epi::Store, out,
-                        w->rows, acc, st);
+                        w->rows, acc, st, c->status.as<int32_t>());
   BN_CUDA(cudaGetLastError());
   return BITNET_OK;
 }

@@ -86,9 +86,22 @@ struct Segments {
 enum class Epi : int { Store = 0, Residual = 1 };
 // out[m][n] = (sum_k W[n,k] x[m][k]) * ((seg_scale*act_absmax[m])/127); Residual: out += that.
 // acc (optional) receives the int32 sums [M][N] (row stride N).
+// `status` (optional) receives kStatusWaitTimeout if the tensor-core kernel
+// (used for M > 64 when ternary_tc_prepare succeeded) gives up a wait.
 void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
                            const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo,
-                           int32_t* acc, cudaStream_t st);
+                           int32_t* acc, cudaStream_t st, int32_t* status = nullptr);
+// tcgen05 ternary GEMM (kernels_tcgen05.cu): 128 weight rows x up to 256
+// activation rows per CTA, TMEM accumulator, optional cluster split-K.
+int ternary_tc_prepare();  // per device, outside graph capture; 0 on success
+size_t ternary_tc_smem();
+// Tile plan for an M x N x K product: activation rows per CTA, activation
+// stages, k splits (cluster size) and k-steps per split. 0 on success.
+int ternary_tc_plan(int N, int K, int M, int* nb, int* stages, int* splits, int* per);
+int launch_ternary_tc(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
+                      const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo, int32_t* acc,
+                      int32_t* status, cudaStream_t st);  // 0 on success
+void set_ternary_tc_ready(bool ready);
 // row_sum for callers that quantised elsewhere.
 void launch_row_sum(const int8_t* xq, int ldq, int M, int K, int32_t* row_sum, cudaStream_t st);
 

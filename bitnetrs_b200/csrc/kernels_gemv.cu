@@ -329,11 +329,17 @@ static void run_mma(const uint32_t* W, int N, int kw, const int8_t* xq, int ldq,
   count_launch();
 }
 
+static bool g_tc_ready = false;  // ternary_tc_prepare succeeded on every device set up so far
+void set_ternary_tc_ready(bool ready) { g_tc_ready = ready; }
+
 void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
                            const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo,
-                           int32_t* acc, cudaStream_t st) {
+                           int32_t* acc, cudaStream_t st, int32_t* status) {
   const int kw = (int)words_per_row(K);
   if (M <= 0 || N <= 0) return;
+  if (M > 64 && status && g_tc_ready &&
+      launch_ternary_tc(W, N, K, xq, ldq, act_absmax, row_sum, M, seg, epi, out, ldo, acc, status, st) == 0)
+    return;
   if (M == 1) {
     const int kw4 = kw / 4;
     const size_t smem = (size_t)kw * 16;

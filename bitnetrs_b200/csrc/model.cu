@@ -254,7 +254,7 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
     sqkv.scale[2] = Lw.sv;
     timed(m, kMatmul, st, [&] {
       launch_ternary_matmul(Lw.wqkv, nqkv, H, m->xq, m->ldq, m->amax, m->rowsum, T, sqkv, Epi::Store, m->qkv, nqkv,
-                            nullptr, st);
+                            nullptr, st, m->status);
     });
     timed(m, kRopeKv, st, [&] {
       launch_rope_kv_store(m->qkv, nqkv, T, m->nh, m->nkv, m->hd, m->rope_cos, m->rope_sin, m->tok_pos, m->tok_seq,
@@ -286,7 +286,7 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
     so.end[0] = so.end[1] = so.end[2] = H;
     so.scale[0] = so.scale[1] = so.scale[2] = Lw.so;
     timed(m, kMatmul, st, [&] {
-      launch_ternary_matmul(Lw.wo, H, qd, m->xq, m->ldq, m->amax, m->rowsum, T, so, Epi::Residual, m->h, H, nullptr, st);
+      launch_ternary_matmul(Lw.wo, H, qd, m->xq, m->ldq, m->amax, m->rowsum, T, so, Epi::Residual, m->h, H, nullptr, st, m->status);
     });
     // FFN block
     timed(m, kNormQuant, st, [&] {
@@ -300,7 +300,7 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
     sgu.scale[1] = sgu.scale[2] = Lw.su;
     timed(m, kMatmul, st, [&] {
       launch_ternary_matmul(Lw.wgu, 2 * F, H, m->xq, m->ldq, m->amax, m->rowsum, T, sgu, Epi::Store, m->gu, 2 * F,
-                            nullptr, st);
+                            nullptr, st, m->status);
     });
     timed(m, kNormQuant, st, [&] {
       launch_norm_quant(m->gu, m->gu + F, 2 * F, Lw.ffn_sub_norm, F, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status,
@@ -311,7 +311,7 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
     sd.scale[0] = sd.scale[1] = sd.scale[2] = Lw.sd;
     timed(m, kMatmul, st, [&] {
       launch_ternary_matmul(Lw.wdown, H, F, m->xq, m->ldq, m->amax, m->rowsum, T, sd, Epi::Residual, m->h, H, nullptr,
-                            st);
+                            st, m->status);
     });
   }
   // final norm on the selected rows, lm_head, greedy argmax

@@ -23,7 +23,7 @@ def unpack_codes(packed, rows, cols):
     return np.where(codes == 0, 1.0, np.where(codes == 2, -1.0, 0.0))
 
 
-@pytest.mark.parametrize("M", [1, 2, 8, 16, 17, 64, 65, 128, 256, 512])
+@pytest.mark.parametrize("M", [1, 2, 8, 16, 17, 64, 65, 128, 200, 256, 512])
 @pytest.mark.parametrize("N_,K", [(2560, 2560), (640, 2560), (2560, 6912), (6912, 2560), (100, 200)])
 def test_device_matmul_bit_exact(cuda_backend, M, N_, K):
     import torch
