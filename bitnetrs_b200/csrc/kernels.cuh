@@ -102,6 +102,11 @@ int launch_ternary_tc(const uint32_t* W, int N, int K, const int8_t* xq, int ldq
                       const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo, int32_t* acc,
                       int32_t* status, cudaStream_t st);  // 0 on success
 void set_ternary_tc_ready(bool ready);
+bool ternary_tc_ready();
+// Tensor-core lm_head (kernels_tcgen05.cu): a3 = [M][3H] bf16 terms of h.
+bool lm_head_tc_supported(int H);
+int launch_lm_head_tc(const uint16_t* a3, int M, int V, int H, const int8_t* W, const float* scales, float* out,
+                      int ldo, int32_t* status, cudaStream_t st);  // 0 on success
 // row_sum for callers that quantised elsewhere.
 void launch_row_sum(const int8_t* xq, int ldq, int M, int K, int32_t* row_sum, cudaStream_t st);
 
@@ -119,7 +124,7 @@ void launch_lm_head(const void* W, LmW wt, const float* scales, const float* h, 
 bool lm_head_mma_supported(int H);
 int lm_head_mma_prepare();  // outside graph capture; 0 on success
 void launch_lm_head_mma(const float* h, int M, int V, int H, const int8_t* W, const float* scales, uint16_t* a3,
-                        float* out, int ldo, cudaStream_t st);
+                        float* out, int ldo, cudaStream_t st, int32_t* status = nullptr);
 // greedy argmax per row (ties -> last index, NaN compares Equal).
 void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cudaStream_t st);
 

@@ -331,6 +331,7 @@ static void run_mma(const uint32_t* W, int N, int kw, const int8_t* xq, int ldq,
 
 static bool g_tc_ready = false;  // ternary_tc_prepare succeeded on every device set up so far
 void set_ternary_tc_ready(bool ready) { g_tc_ready = ready; }
+bool ternary_tc_ready() { return g_tc_ready; }
 
 void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
                            const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo,

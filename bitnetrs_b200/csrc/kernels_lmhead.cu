@@ -278,9 +278,15 @@ int lm_head_mma_prepare() {
 }
 
 void launch_lm_head_mma(const float* h, int M, int V, int H, const int8_t* W, const float* scales, uint16_t* a3,
-                        float* out, int ldo, cudaStream_t st) {
+                        float* out, int ldo, cudaStream_t st, int32_t* status) {
   if (M <= 0 || V <= 0) return;
   split_bf16x3_kernel<<<M, 256, 0, st>>>(h, H, a3);
+  // tcgen05 kernel (same exact products, f32 sums in the tensor core's order)
+  if (status && ternary_tc_ready() && lm_head_tc_supported(H) &&
+      launch_lm_head_tc(a3, M, V, H, W, scales, out, ldo, status, st) == 0) {
+    count_launch();  // the split kernel
+    return;
+  }
   int smem = kLmStages * (kLmBM * kLmAS + kLmBN * kLmWS);
   dim3 grid((unsigned)ceil_div(M, kLmBM), (unsigned)ceil_div(V, kLmBN));
   lm_head_mma_kernel<<<grid, 256, smem, st>>>(a3, W, scales, M, V, H, out, ldo);

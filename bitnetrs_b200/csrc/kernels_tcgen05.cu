@@ -1,8 +1,14 @@
-// kernels_tcgen05.cu — ternary x int8 GEMM on the 5th-generation tensor
-// cores (tcgen05.mma kind::i8, accumulator in tensor memory) for M > 64
-// activation rows (batched decode and prefill).
+// kernels_tcgen05.cu — weight-streaming GEMMs on the 5th-generation tensor
+// cores (tcgen05.mma, accumulator in tensor memory) for many activation rows:
+//   * the ternary x int8 matmul (kind::i8) for M > 64 rows (batched decode
+//     and prefill);
+//   * the int8 lm_head for many rows (kind::f16): every int8 weight is exact
+//     in bf16 and the f32 hidden state is the sum of three bf16 terms
+//     (h1 | h2 | h3, concatenated along K), so each product the tensor core
+//     forms is exact and only the f32 summation order differs from the
+//     reference's FMA chains (the AUTO numerics of the lm_head).
 //
-// Same integer identity as the other matmul kernels (gemv.rs:299-308):
+// Ternary: the same integer identity as the other matmul kernels (gemv.rs:299-308):
 //     sum_k (1 - c_k) x_k = rowsum(x) - sum_k c_k x_k,   c_k in {0,1,2},
 // so the tensor core multiplies unsigned 2-bit codes widened to u8 by the
 // signed int8 activations, exact in int32; the epilogue applies the
@@ -52,7 +58,6 @@ namespace {
 constexpr int kTcRows = 128;    // weight rows per CTA: MMA M, TMEM lanes
 constexpr int kTcBK = 128;      // codes per k-step (128 bytes of u8 per row)
 constexpr int kTcMaxNb = 256;   // activation rows per CTA: MMA N
-constexpr int kTcGroup = 4;     // k-steps per packed-weight load (128 bytes per row)
 constexpr int kTcPG = 4;        // packed-weight ring (groups)
 constexpr int kTcMaxSB = 8;     // k-step stages (activation tile + widened weights; fewer for wide tiles)
 constexpr int kTcThreads = 192; // warps 0-3 widen + epilogue, warp 4 loads, warp 5 MMA
@@ -123,11 +128,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
   return d;
 }
-// Instruction descriptor: D s32, A u8 (codes), B s8 (activations), both
-// K-major, M = 128, N = nb.
-__device__ __forceinline__ uint32_t tc_idesc(int nb) {
-  return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(nb >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
-}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -179,17 +179,88 @@ __device__ __forceinline__ void store_rows(float* __restrict__ p, int ldo, const
   }
 }
 
+// int8 (sign-extended) -> float, exactly, on the full-rate pipes: the bit
+// pattern 0x4B400000 + v is the float 1.5 * 2^23 + v for |v| < 2^22.
+__device__ __forceinline__ float i8_exact_f32(int32_t v) {
+  return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+// Four int8 of a word (lowest byte first) -> two bf16x2 words; a float holding
+// an integer of at most 8 significant bits has its bf16 in the top half.
+__device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t w) {
+  const float f0 = i8_exact_f32((int32_t)(w << 24) >> 24), f1 = i8_exact_f32((int32_t)(w << 16) >> 24);
+  const float f2 = i8_exact_f32((int32_t)(w << 8) >> 24), f3 = i8_exact_f32((int32_t)w >> 24);
+  return make_uint2((__float_as_uint(f0) >> 16) | (__float_as_uint(f1) & 0xffff0000u),
+                    (__float_as_uint(f2) >> 16) | (__float_as_uint(f3) & 0xffff0000u));
+}
+
 }  // namespace
+
+enum class TcKind : int { Ternary = 0, LmHead = 1 };
+
+// Per-kind pieces of the kernel. A weight load brings 128 bytes of each of the
+// tile's 128 rows (128-byte swizzled); a k-step fills 32 TMEM columns.
+template <TcKind K>
+struct TcTraits;
+template <>
+struct TcTraits<TcKind::Ternary> {
+  static constexpr int kGroupSteps = 4;  // 4 x 32 bytes of packed codes per load
+  static constexpr int kActCols = 128;   // int8 activation elements per k-step
+  // D s32, A u8 (codes), B s8 (activations), both K-major, M = 128, N = nb.
+  static __device__ __forceinline__ uint32_t idesc(int nb) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(nb >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+  }
+  // step q of the group: chunks 2q, 2q+1 of the row's packed line. Word c holds
+  // codes 16c..16c+15; column 4c+e receives codes 16c+4e..16c+4e+3.
+  static __device__ __forceinline__ void widen(const uint8_t* prow, int q, int row, uint32_t (&col)[32]) {
+    const uint4 p0 = *reinterpret_cast<const uint4*>(prow + (((2 * q) ^ (row & 7)) << 4));
+    const uint4 p1 = *reinterpret_cast<const uint4*>(prow + (((2 * q + 1) ^ (row & 7)) << 4));
+    const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) col[4 * c + e] = (words[c] >> (2 * e)) & 0x03030303u;
+    }
+  }
+};
+template <>
+struct TcTraits<TcKind::LmHead> {
+  static constexpr int kGroupSteps = 2;  // 2 x 64 int8 weights per load
+  static constexpr int kActCols = 64;    // bf16 activation elements per k-step
+  // D f32, A bf16 (widened weights), B bf16 (activation terms), K-major, M = 128, N = nb.
+  static __device__ __forceinline__ uint32_t idesc(int nb) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nb >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+  }
+  // step q of the group: chunks 4q..4q+3 (64 int8); column c receives
+  // elements 2c, 2c+1 as bf16x2.
+  static __device__ __forceinline__ void widen(const uint8_t* prow, int q, int row, uint32_t (&col)[32]) {
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const uint4 p = *reinterpret_cast<const uint4*>(prow + (((4 * q + cc) ^ (row & 7)) << 4));
+      const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint2 b = i8x4_to_bf16x4(w[j]);
+        col[8 * cc + 2 * j] = b.x;
+        col[8 * cc + 2 * j + 1] = b.y;
+      }
+    }
+  }
+};
 
 struct TcShape {
   int nb, sb, splits, per;  // activation rows per CTA, activation stages, k splits, k-steps per split
 };
 
+// nk k-steps in all; the lm_head runs three passes of kpass k-steps over the
+// same weights (one per bf16 term of the activations), the ternary matmul one.
+template <TcKind KIND>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    ternary_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, int N,
-                      int nk, int M, TcShape sh, const float* __restrict__ amax, const int32_t* __restrict__ rowsum,
-                      Segments seg, Epi epi, float* __restrict__ out, int ldo, int32_t* __restrict__ acc_out,
-                      int32_t* __restrict__ status) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, int N, int nk,
+                   int kpass, int M, TcShape sh, const float* __restrict__ amax, const int32_t* __restrict__ rowsum,
+                   Segments seg, const float* __restrict__ vscale, Epi epi, float* __restrict__ out, int ldo,
+                   int32_t* __restrict__ acc_out, int32_t* __restrict__ status) {
+  using Tr = TcTraits<KIND>;
+  constexpr int kGroup = Tr::kGroupSteps;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t pk_full[kTcPG], pk_empty[kTcPG];
   __shared__ __align__(8) uint64_t full[kTcMaxSB], empty[kTcMaxSB];
@@ -208,7 +279,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (splits > 1) asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(rank));
   const int kb = (int)rank * sh.per;
   const int steps = max(0, min(nk, kb + sh.per) - kb);
-  // shared layout (1024-aligned): activation stages | packed ring
+  // shared layout (1024-aligned): activation stages | weight ring
   const uint32_t raw = su32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   const int act_bytes = nb * kTcBK;
@@ -255,13 +326,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int s = 0, wrap = 0;  // stage of step i; completed passes over the ring
     for (int i = 0; i < steps; ++i) {
       if (__any_sync(0xffffffffu, *abort_p != 0)) break;
-      if ((i & (kTcGroup - 1)) == 0) {
-        const int g = i / kTcGroup, sp = g % kTcPG;
+      if ((i & (kGroup - 1)) == 0) {
+        const int g = i / kGroup, sp = g % kTcPG;
         if (g >= kTcPG && !__all_sync(0xffffffffu, tc_wait(su32(&pk_empty[sp]), ((g / kTcPG) - 1) & 1, abort_p))) {
           stop = true;
           break;
         }
-        if (lane == 0) tc_load_2d(sPk32 + sp * kTcPacked, &wmap, (kb + i) * 8, n0, su32(&pk_full[sp]), kTcPacked);
+        // x of the group's first k-step: packed words (ternary) or weight bytes within the pass
+        const int wx = KIND == TcKind::Ternary ? (kb + i) * 8 : ((kb + i) % kpass) * 64;
+        if (lane == 0) tc_load_2d(sPk32 + sp * kTcPacked, &wmap, wx, n0, su32(&pk_full[sp]), kTcPacked);
         __syncwarp();
         g_issued = g + 1;
       }
@@ -270,7 +343,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       if (lane == 0)
-        tc_load_2d(sAct32 + s * act_bytes, &xmap, (kb + i) * kTcBK, m0, su32(&full[s]), (uint32_t)act_bytes);
+        tc_load_2d(sAct32 + s * act_bytes, &xmap, (kb + i) * Tr::kActCols, m0, su32(&full[s]), (uint32_t)act_bytes);
       __syncwarp();
       a_issued = i + 1;
       if (++s == sb) {
@@ -290,7 +363,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 5) {
     // ---------------- MMA issue: the whole warp runs the loop, lane 0 issues ----------------
-    const uint32_t idesc = tc_idesc(nb);
+    const uint32_t idesc = Tr::idesc(nb);
     int s = 0;
     uint32_t parity = 0;
     bool ok = steps > 0 && tc_wait(su32(&full[0]), 0, abort_p);
@@ -307,11 +380,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int kk = 0; kk < kTcBK / 32; ++kk) {
           const uint64_t bd = sw128_desc(b_addr + 32 * kk);
           const uint32_t accumulate = (i > 0 || kk > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-              " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
-              "r"(a_tmem + 8u * kk), "l"(bd), "r"(idesc), "r"(accumulate)
-              : "memory");
+          if constexpr (KIND == TcKind::Ternary)
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+                "r"(a_tmem + 8u * kk), "l"(bd), "r"(idesc), "r"(accumulate)
+                : "memory");
+          else  // bf16 x bf16 -> f32 (A and B of one type)
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+                "r"(a_tmem + 8u * kk), "l"(bd), "r"(idesc), "r"(accumulate)
+                : "memory");
         }
       }
       __syncwarp();
@@ -329,19 +409,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     // epilogue constants, read after the named barrier that precedes the
     // epilogue; their loads overlap the first weight loads
-    for (int c = tid; c < kTcMaxNb; c += 128) {
-      const int m = m0 + c;
-      const bool valid = c < nb && m < M;
-      const float am = valid ? amax[m] : 0.0f;
-      rs_s[c] = valid ? rowsum[m] : 0;
+    if constexpr (KIND == TcKind::Ternary) {
+      for (int c = tid; c < kTcMaxNb; c += 128) {
+        const int m = m0 + c;
+        const bool valid = c < nb && m < M;
+        const float am = valid ? amax[m] : 0.0f;
+        rs_s[c] = valid ? rowsum[m] : 0;
 #pragma unroll
-      for (int q = 0; q < 3; ++q) comb_s[q][c] = __fdiv_rn(__fmul_rn(seg.scale[q], am), 127.0f);
+        for (int q = 0; q < 3; ++q) comb_s[q][c] = __fdiv_rn(__fmul_rn(seg.scale[q], am), 127.0f);
+      }
     }
     // ---------------- widen: thread tid owns weight row n0 + tid (TMEM lane tid) ----------------
     const uint32_t wlane = tmem + ((uint32_t)(32 * warp) << 16) + kTcTmemA;
     int s = 0, wrap = 0;
     for (int i = 0; i < steps; ++i) {
-      const int g = i / kTcGroup, q = i & (kTcGroup - 1), sp = g % kTcPG;
+      const int g = i / kGroup, q = i & (kGroup - 1), sp = g % kTcPG;
       bool ok = true;
       if (q == 0) ok = tc_wait(su32(&pk_full[sp]), (g / kTcPG) & 1, abort_p);
       if (ok && wrap > 0) ok = tc_wait(su32(&empty[s]), (wrap - 1) & 1, abort_p);
@@ -349,22 +431,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         fail();
         break;
       }
-      // the four k-steps of a group are the 16-byte chunks 2q, 2q+1 of the
-      // row's 128-byte packed line, stored 128-byte swizzled
-      const uint8_t* prow = sPk + sp * kTcPacked + tid * 128;
-      const uint4 p0 = *reinterpret_cast<const uint4*>(prow + (((2 * q) ^ (tid & 7)) << 4));
-      const uint4 p1 = *reinterpret_cast<const uint4*>(prow + (((2 * q + 1) ^ (tid & 7)) << 4));
-      if (q == kTcGroup - 1 || i == steps - 1) {
+      // this row's 128-byte weight line, stored 128-byte swizzled
+      uint32_t col[32];
+      Tr::widen(sPk + sp * kTcPacked + tid * 128, q, tid, col);
+      if (q == kGroup - 1 || i == steps - 1) {
         __syncwarp();
         if (lane == 0) tc_arrive(su32(&pk_empty[sp]));
-      }
-      const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-      // word c holds codes 16c..16c+15; column 4c+e receives codes 16c+4e..16c+4e+3
-      uint32_t col[32];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) col[4 * c + e] = (words[c] >> (2 * e)) & 0x03030303u;
       }
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");  // after the empty wait
       tmem_st32(wlane + (uint32_t)(s * (kTcBK / 4)), col);
@@ -387,7 +459,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int sidx = n < seg.end[0] ? 0 : (n < seg.end[1] ? 1 : 2);
     const float* comb = comb_s[sidx];
     const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-    if (splits == 1) {
+    if constexpr (KIND == TcKind::LmHead) {
+      // logits[m][n] = acc * scale[n]
+      const bool live = ok && n < N;
+      const float vs = live ? vscale[n] : 0.0f;
+      const int rows = min(nb, M - m0);
+#pragma unroll 1
+      for (int c0 = 0; c0 < nb; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(trow + (uint32_t)c0, r);
+        const int cnt = min(32, rows - c0);
+        if (live && cnt > 0) {
+          float* p = out + (size_t)(m0 + c0) * ldo + n;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < cnt) p[(size_t)j * ldo] = __fmul_rn(__uint_as_float(r[j]), vs);
+        }
+      }
+    } else if (splits == 1) {
       const bool live = ok && n < N;
       const int rows = min(nb, M - m0);  // valid activation rows of this tile
 #pragma unroll 1
@@ -423,7 +512,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   }
 
-  if (splits > 1) {
+  if (KIND == TcKind::Ternary && splits > 1) {
     // every thread of every CTA of the cluster meets both barriers
     cluster_sync_all();
     if (tid < 128) {
@@ -508,8 +597,11 @@ int ternary_tc_prepare() {
   if (!tc_encoder()) return 1;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
-  return cudaFuncSetAttribute(ternary_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcDynBudget) ==
-                 cudaSuccess
+  if (cudaFuncSetAttribute(tc_gemm_kernel<TcKind::Ternary>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kTcDynBudget) != cudaSuccess)
+    return 1;
+  return cudaFuncSetAttribute(tc_gemm_kernel<TcKind::LmHead>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kTcDynBudget) == cudaSuccess
              ? 0
              : 1;
 }
@@ -584,9 +676,51 @@ int launch_ternary_tc(const uint32_t* W, int N, int K, const int8_t* xq, int ldq
   attr[0].val.clusterDim.z = (unsigned)sh.splits;
   cfg.attrs = attr;
   cfg.numAttrs = sh.splits > 1 ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, ternary_tc_kernel, wmap, xmap, N, nk, M, sh, act_absmax, row_sum, seg, epi, out, ldo,
-                         acc, status) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, tc_gemm_kernel<TcKind::Ternary>, wmap, xmap, N, nk, nk, M, sh, act_absmax, row_sum,
+                         seg, static_cast<const float*>(nullptr), epi, out, ldo, acc, status) != cudaSuccess)
     return 1;
+  count_launch();
+  return 0;
+}
+
+bool lm_head_tc_supported(int H) { return H > 0 && H % 128 == 0; }
+
+int launch_lm_head_tc(const uint16_t* a3, int M, int V, int H, const int8_t* W, const float* scales, float* out,
+                      int ldo, int32_t* status, cudaStream_t st) {
+  auto enc = tc_encoder();
+  if (!enc || !status || !lm_head_tc_supported(H) || M < 1 || V < 1) return 1;
+  if ((reinterpret_cast<uintptr_t>(a3) & 15) || (reinterpret_cast<uintptr_t>(W) & 15)) return 1;
+  TcShape sh;
+  // rows per CTA and stages as for the ternary matmul of the same M; no k split
+  if (ternary_tc_plan(V, 16, M, &sh.nb, &sh.sb, &sh.splits, &sh.per) != 0) return 1;
+  const int kpass = H / 64, nk = 3 * kpass;
+  sh.splits = 1;
+  sh.per = nk;
+  CUtensorMap xmap, wmap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)(3 * H), (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)(3 * H) * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)sh.nb};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a3), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return 1;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)V};
+    const cuuint64_t strides[1] = {(cuuint64_t)H};
+    const cuuint32_t box[2] = {128, (cuuint32_t)kTcRows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(W), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return 1;
+  }
+  Segments seg;
+  dim3 grid((unsigned)ceil_div(V, kTcRows), (unsigned)ceil_div(M, sh.nb), 1);
+  tc_gemm_kernel<TcKind::LmHead><<<grid, kTcThreads, tc_dyn_smem(sh.nb, sh.sb), st>>>(
+      wmap, xmap, V, nk, kpass, M, sh, nullptr, nullptr, seg, scales, Epi::Store, out, ldo, nullptr, status);
   count_launch();
   return 0;
 }

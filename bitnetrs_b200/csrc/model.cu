@@ -323,7 +323,7 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
   });
   timed(m, kLmHead, st, [&] {
     if (use_fast_lm_head(m, n_out))
-      launch_lm_head_mma(m->hn, n_out, m->V, H, m->lm_i8, m->lm_scales, m->a3, m->logits, m->V, st);
+      launch_lm_head_mma(m->hn, n_out, m->V, H, m->lm_i8, m->lm_scales, m->a3, m->logits, m->V, st, m->status);
     else
       launch_lm_head(m->lm_i8, LmW::I8, m->lm_scales, m->hn, H, n_out, m->V, H, m->logits, m->V, st);
   });

@@ -207,6 +207,31 @@ def hd128():
     return cfg, synth.random_model(cfg, seed=21)
 
 
+def test_many_row_lm_head_auto(cuda_backend, hd128):
+    """AUTO numerics with more than 16 output rows: the lm_head runs on the
+    tensor cores (exact products, f32 sums in the tensor core's order) and
+    the logits of every row stay at f32-level agreement with the oracle."""
+    cfg, w = hd128
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=64)
+    om = O.OracleModel(w)
+    lens = [1 + 37 * i for i in range(40)]
+    seqs = list(range(len(lens)))
+    toks = synth.uniform_u32(17, 4, len(lens), 0, cfg.vocab_size - 1).tolist()
+    ctx = [synth.kv_normal(43, s, cfg, n) for s, n in zip(seqs, lens)]
+    kv = m.new_kv_cache(num_pages=sum((n + 20) // 16 for n in lens) + 8, max_seqs=len(lens), kv_dtype=KV_BF16)
+    for s, (k, v) in zip(seqs, ctx):
+        kv.write(s, k, v)
+    nxt, logits = m.decode_step(kv, seqs, toks, want_logits=True)
+    for i, s in enumerate(seqs):
+        okv = om.kv(lens[i] + 4, bf16=True)
+        okv.seed(*ctx[i])
+        r = om.forward(okv, [toks[i]], lens[i])
+        close_logits(logits[i], r, tol=1e-5)
+        top2 = np.partition(r, -2)[-2:]
+        if top2[1] - top2[0] > 1e-4 * np.max(np.abs(r)):
+            assert nxt[i] == O.lib().orc_greedy_argmax(O.p(r), r.size)
+
+
 @pytest.mark.parametrize("lens", [[100, 300, 513, 1000, 1, 256, 257, 1500]])
 def test_fast_numerics_one_step(cuda_backend, hd128, lens):
     """One decode step from identical seeded state: the tensor-core attention
