@@ -208,6 +208,175 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   quantize_row_smem(row, d, xq + (size_t)m * ldq, ldq, act_absmax + m, nullptr, row_sum + m, status, red_f, red_i);
 }
 
+// Register-resident variant for rows of at most 8192 values (d % 4 == 0):
+// thread t holds float4 groups t, t + 256, ... of the row. The norm weights
+// (no kernel writes them) are loaded before griddepcontrol.wait; lanes 0..7 of
+// warp 0 run the eight FMA chains from a shared copy of the row, their
+// shared-memory loads issued one block of 16 ahead; the rest of the block then
+// normalises, takes the absmax and quantises from registers. Same operations
+// and order as norm_quant_kernel.
+template <bool GATE_UP, int U>
+__global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __restrict__ x, const float* __restrict__ x2,
+                                                             int ldx, const float* __restrict__ w, int d, float eps,
+                                                             int8_t* __restrict__ xq, int ldq,
+                                                             float* __restrict__ act_absmax,
+                                                             int32_t* __restrict__ row_sum, int32_t* status) {
+  extern __shared__ float4 row4[];  // the row, d / 4 float4
+  __shared__ float bc;
+  __shared__ float red_f[8];
+  __shared__ int red_i[8], red_b[8];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int m = blockIdx.x, n4 = d >> 2;
+  pdl_launch_dependents();
+  float4 wv[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int j = t + 256 * u;
+    wv[u] = j < n4 ? reinterpret_cast<const float4*>(w)[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  pdl_wait();
+  const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)m * ldx);
+  const float4* y4 = GATE_UP ? reinterpret_cast<const float4*>(x2 + (size_t)m * ldx) : nullptr;
+  float4 v[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int j = t + 256 * u;
+    v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (j < n4) {
+      float4 a = x4[j];
+      if (GATE_UP) {
+        const float4 b = y4[j];
+        const float r0 = fmaxf(a.x, 0.0f), r1 = fmaxf(a.y, 0.0f), r2 = fmaxf(a.z, 0.0f), r3 = fmaxf(a.w, 0.0f);
+        a = make_float4(__fmul_rn(__fmul_rn(r0, r0), b.x), __fmul_rn(__fmul_rn(r1, r1), b.y),
+                        __fmul_rn(__fmul_rn(r2, r2), b.z), __fmul_rn(__fmul_rn(r3, r3), b.w));
+      }
+      v[u] = a;
+      row4[j] = a;
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float* row = reinterpret_cast<const float*>(row4);
+    const int chunks = d >> 3;
+    float acc = 0.0f;
+    if (lane < 8) {
+      const int full = chunks & ~15;
+      float cur[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) cur[k] = full ? row[8 * k + lane] : 0.0f;
+      int i = 0;
+      for (; i < full; i += 16) {
+        float nxt[16];
+        const int ni = i + 16 < full ? i + 16 : i;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) nxt[k] = row[8 * (ni + k) + lane];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(cur[k], cur[k], acc);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
+      }
+      for (; i < chunks; ++i) {
+        const float a = row[8 * i + lane];
+        acc = __fmaf_rn(a, a, acc);
+      }
+    }
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, acc, j);
+    if (lane == 0) {
+      float ss = hsum8(a);
+      for (int i = chunks * 8; i < d; ++i) ss = __fadd_rn(ss, __fmul_rn(row[i], row[i]));
+      const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps));
+      bc = __fdiv_rn(1.0f, rms);
+    }
+  }
+  __syncthreads();
+  const float inv = bc;
+  float mx = 0.0f;
+  int bad = 0;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (t + 256 * u < n4) {
+      float4 a = v[u];
+      a.x = __fmul_rn(__fmul_rn(a.x, inv), wv[u].x);
+      a.y = __fmul_rn(__fmul_rn(a.y, inv), wv[u].y);
+      a.z = __fmul_rn(__fmul_rn(a.z, inv), wv[u].z);
+      a.w = __fmul_rn(__fmul_rn(a.w, inv), wv[u].w);
+      v[u] = a;
+      bad |= !isfinite(a.x) || !isfinite(a.y) || !isfinite(a.z) || !isfinite(a.w);
+      mx = fmaxf(fmaxf(fmaxf(mx, fabsf(a.x)), fmaxf(fabsf(a.y), fabsf(a.z))), fabsf(a.w));
+    }
+  }
+  mx = warp_max(mx);
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) {
+    red_f[warp] = mx;
+    red_b[warp] = bad;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    mx = fmaxf(mx, red_f[k]);
+    bad |= red_b[k];
+  }
+  const float mc = fmaxf(mx, 1e-5f);
+  const float scale = __fdiv_rn(mc, 127.0f), qinv = __fdiv_rn(127.0f, mc);
+  int8_t* q = xq + (size_t)m * ldq;
+  int sum = 0;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int j = t + 256 * u;
+    if (j < n4) {
+      const int8_t c0 = quant_i8(v[u].x, qinv), c1 = quant_i8(v[u].y, qinv), c2 = quant_i8(v[u].z, qinv),
+                   c3 = quant_i8(v[u].w, qinv);
+      sum += (int)c0 + (int)c1 + (int)c2 + (int)c3;
+      reinterpret_cast<char4*>(q)[j] = make_char4(c0, c1, c2, c3);
+    }
+  }
+  for (int i = d + t; i < ldq; i += 256) q[i] = 0;  // K padding of the int8 row
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) red_i[warp] = sum;
+  __syncthreads();
+  if (t == 0) {
+    int total = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) total += red_i[k];
+    act_absmax[m] = __fmul_rn(scale, 127.0f);
+    row_sum[m] = total;
+    if (bad && status) atomicOr(status, 1);
+  }
+}
+
+template <bool GATE_UP>
+static bool launch_norm_quant_reg(const float* x, const float* x2, int ldx, const float* w, int d, float eps,
+                                  int8_t* xq, int ldq, float* act_absmax, int32_t* row_sum, int32_t* status, int M,
+                                  cudaStream_t st) {
+  const int n4 = d / 4, U = (n4 + 255) / 256;
+  const bool ok = d % 4 == 0 && ldx % 4 == 0 && ldq % 4 == 0 && U >= 1 && U <= 8 &&
+                  ((uintptr_t)x & 15) == 0 && (!GATE_UP || ((uintptr_t)x2 & 15) == 0) && ((uintptr_t)w & 15) == 0 &&
+                  ((uintptr_t)xq & 3) == 0;
+  if (!ok) return false;
+  const size_t smem = (size_t)d * sizeof(float);
+#define BN_NQ(UU)                                                                                            \
+  case UU:                                                                                                   \
+    norm_quant_reg_kernel<GATE_UP, UU><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, \
+                                                           status);                                          \
+    break;
+  switch (U) {
+    BN_NQ(1)
+    BN_NQ(2)
+    BN_NQ(3)
+    BN_NQ(4)
+    BN_NQ(5)
+    BN_NQ(6)
+    BN_NQ(7)
+    BN_NQ(8)
+  }
+#undef BN_NQ
+  return true;
+}
+
 int row_kernels_prepare() {
   const int bytes = kMaxRowFloats * (int)sizeof(float);
   int bad = 0;
@@ -222,12 +391,15 @@ int row_kernels_prepare() {
 void launch_norm_quant(const float* x, const float* x2, int ldx, const float* w, int d, float eps, int8_t* xq, int ldq,
                        float* act_absmax, int32_t* row_sum, int32_t* status, int M, cudaStream_t st) {
   if (M <= 0) return;
+  count_launch();
+  if (x2 ? launch_norm_quant_reg<true>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status, M, st)
+         : launch_norm_quant_reg<false>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status, M, st))
+    return;
   size_t smem = (size_t)d * sizeof(float);
   if (x2)
     norm_quant_kernel<true><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
   else
     norm_quant_kernel<false><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, status);
-  count_launch();
 }
 
 // ---------------------------------------------------------------------------
