@@ -190,8 +190,19 @@ __device__ __forceinline__ float exp_host_libm(float x, const ExpTable& t) {
 // kernel launched without the attribute.  Measured on the 2B decode step,
 // only the M = 1 GEMV gains from being launched this way (its weight stream
 // starts under the previous kernel); the decode-chain kernels before it call
-// pdl_launch_dependents so that it can.
+// pdl_launch_dependents so that it can. Launching the norm, RoPE and attention
+// kernels this way as well was slower at batch 1 (517 vs 600 tokens/s) and at
+// batch 256.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+// A pointer to data an earlier kernel writes, made opaque after pdl_wait():
+// loads through it depend on an instruction that follows the wait, so the
+// compiler cannot schedule them before it (it may move loads through
+// const __restrict__ pointers across a plain memory clobber).
+template <typename T>
+__device__ __forceinline__ T* after_wait(T* p) {
+  asm volatile("" : "+l"(p)::"memory");
+  return p;
+}
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
 // Rust f32::round: half away from zero (roundf), then clamp, then cast.

@@ -102,6 +102,10 @@ __global__ void rope_kv_store_kernel(const float* __restrict__ qkv, int ldqkv, i
                                      float* __restrict__ q_out) {
   pdl_launch_dependents();
   pdl_wait();
+  qkv = after_wait(qkv);
+  tok_pos = after_wait(tok_pos);
+  tok_seq = after_wait(tok_seq);
+  page_table = after_wait(page_table);
   const int t = blockIdx.x;
   const int pos = tok_pos[t], seq = tok_seq[t];
   const int half = hd / 2;

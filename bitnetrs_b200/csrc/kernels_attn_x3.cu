@@ -158,6 +158,10 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
   const int t = blockIdx.x, kvh = blockIdx.y;
   pdl_launch_dependents();
   pdl_wait();
+  q = after_wait(q);
+  tok_pos = after_wait(tok_pos);
+  tok_seq = after_wait(tok_seq);
+  page_table = after_wait(page_table);
   const int ctx = tok_pos[t] + 1;
   if (ctx > cap || ctx <= 0) {  // uniform over the block
     if (tid == 0) atomicOr(status, kStatusBadContext);

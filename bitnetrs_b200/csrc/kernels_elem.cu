@@ -175,6 +175,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   __shared__ int red_i[32];
   pdl_launch_dependents();
   pdl_wait();
+  x = after_wait(x);
+  if (GATE_UP) x2 = after_wait(x2);
   const int m = blockIdx.x;
   const float* xr = x + (size_t)m * ldx;
   const bool vec = (d & 3) == 0 && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0 && (!GATE_UP || ((uintptr_t)x2 & 15) == 0);
@@ -235,6 +237,8 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
     wv[u] = j < n4 ? reinterpret_cast<const float4*>(w)[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
   pdl_wait();
+  x = after_wait(x);
+  if (GATE_UP) x2 = after_wait(x2);
   const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)m * ldx);
   const float4* y4 = GATE_UP ? reinterpret_cast<const float4*>(x2 + (size_t)m * ldx) : nullptr;
   float4 v[U];
@@ -358,10 +362,10 @@ static bool launch_norm_quant_reg(const float* x, const float* x2, int ldx, cons
                   ((uintptr_t)xq & 3) == 0;
   if (!ok) return false;
   const size_t smem = (size_t)d * sizeof(float);
-#define BN_NQ(UU)                                                                                            \
-  case UU:                                                                                                   \
-    norm_quant_reg_kernel<GATE_UP, UU><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax, row_sum, \
-                                                           status);                                          \
+#define BN_NQ(UU)                                                                                        \
+  case UU:                                                                                               \
+    norm_quant_reg_kernel<GATE_UP, UU><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax,   \
+                                                           row_sum, status);                             \
     break;
   switch (U) {
     BN_NQ(1)

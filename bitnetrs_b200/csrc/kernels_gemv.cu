@@ -86,6 +86,9 @@ __global__ void __launch_bounds__(256) gemv_m1_kernel(const uint32_t* __restrict
       w[r][j] = (row0 + r < N && c < kw4) ? __ldcs(W4 + (size_t)(row0 + r) * kw4 + c) : make_uint4(0, 0, 0, 0);
     }
   pdl_wait();  // weights are constant; x and out belong to the previous kernels
+  xq = after_wait(xq);
+  amax = after_wait(amax);
+  out = after_wait(out);
   int xsum = 0;
   const uint4* xg = reinterpret_cast<const uint4*>(xq);
   for (int i = threadIdx.x; i < kw; i += 256) {
@@ -226,6 +229,10 @@ __global__ void __launch_bounds__(WARPS_M* WARPS_N * 32)
   uint8_t* wsm = smem + STAGES * BM * XS;
   pdl_launch_dependents();
   pdl_wait();
+  X = after_wait(X);
+  amax = after_wait(amax);
+  rowsum = after_wait(rowsum);
+  out = after_wait(out);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wm = warp / WARPS_N, wn = warp % WARPS_N;
