@@ -468,7 +468,7 @@ def run_cuda(a):
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": attn_bytes,
                          "avg_launch_ms": attn_launch_ms},
             "gemv_m1": gemv_m1,
-            "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32, mma.sync)", "ms_per_step": mm_ms,
+            "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32; tcgen05 kind::i8 for the batch-256 step, dp4a GEMV at batch 1)", "ms_per_step": mm_ms,
                      "launches": mm_n, "hbm_gbs": (w_bytes + act_bytes) / (mm_ms / 1e3) / 1e9 if mm_ms else None,
                      "tops": mm_ops / (mm_ms / 1e3) / 1e12 if mm_ms else None},
             "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kt.items()},
