@@ -94,7 +94,6 @@ void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, in
 // tcgen05 ternary GEMM (kernels_tcgen05.cu): 128 weight rows x up to 256
 // activation rows per CTA, TMEM accumulator, optional cluster split-K.
 int ternary_tc_prepare();  // per device, outside graph capture; 0 on success
-size_t ternary_tc_smem();
 // Tile plan for an M x N x K product: activation rows per CTA, activation
 // stages, k splits (cluster size) and k-steps per split. 0 on success.
 int ternary_tc_plan(int N, int K, int M, int* nb, int* stages, int* splits, int* per);

@@ -591,8 +591,6 @@ size_t tc_dyn_smem(int nb, int sb) { return 1024 + (size_t)sb * nb * kTcBK + (si
 int g_sm_count = 148;
 }  // namespace
 
-size_t ternary_tc_smem() { return kTcDynBudget; }
-
 int ternary_tc_prepare() {
   if (!tc_encoder()) return 1;
   int dev = 0;
@@ -677,8 +675,10 @@ int launch_ternary_tc(const uint32_t* W, int N, int K, const int8_t* xq, int ldq
   cfg.attrs = attr;
   cfg.numAttrs = sh.splits > 1 ? 1 : 0;
   if (cudaLaunchKernelEx(&cfg, tc_gemm_kernel<TcKind::Ternary>, wmap, xmap, N, nk, nk, M, sh, act_absmax, row_sum,
-                         seg, static_cast<const float*>(nullptr), epi, out, ldo, acc, status) != cudaSuccess)
+                         seg, static_cast<const float*>(nullptr), epi, out, ldo, acc, status) != cudaSuccess) {
+    (void)cudaGetLastError();  // the caller falls back to another kernel; do not leave the error pending
     return 1;
+  }
   count_launch();
   return 0;
 }
@@ -719,8 +719,17 @@ int launch_lm_head_tc(const uint16_t* a3, int M, int V, int H, const int8_t* W, 
   }
   Segments seg;
   dim3 grid((unsigned)ceil_div(V, kTcRows), (unsigned)ceil_div(M, sh.nb), 1);
-  tc_gemm_kernel<TcKind::LmHead><<<grid, kTcThreads, tc_dyn_smem(sh.nb, sh.sb), st>>>(
-      wmap, xmap, V, nk, kpass, M, sh, nullptr, nullptr, seg, scales, Epi::Store, out, ldo, nullptr, status);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = tc_dyn_smem(sh.nb, sh.sb);
+  cfg.stream = st;
+  if (cudaLaunchKernelEx(&cfg, tc_gemm_kernel<TcKind::LmHead>, wmap, xmap, V, nk, kpass, M, sh,
+                         static_cast<const float*>(nullptr), static_cast<const int32_t*>(nullptr), seg, scales,
+                         Epi::Store, out, ldo, static_cast<int32_t*>(nullptr), status) != cudaSuccess) {
+    (void)cudaGetLastError();  // the caller falls back to the mma.sync kernel
+    return 1;
+  }
   count_launch();
   return 0;
 }
