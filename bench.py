@@ -48,6 +48,7 @@ def args():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv-sweep", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the C3 ragged-prefill measurement")
     # smaller contexts keep profiler captures of the same kernels to a few GB
     ap.add_argument("--ctx-hi", type=int, default=CTX_HI, help="largest seeded context (default C4's 4096)")
     return ap.parse_args()
@@ -288,6 +289,61 @@ def run_reference(a):
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
+PREFILL_SEQS, PREFILL_LO, PREFILL_HI = 64, 32, 2048  # C3: 64 prompts, lengths U[32, 2048]
+PREFILL_CHUNK = 1024  # tokens per step: the largest step that keeps reference-order attention
+TERNARY_OPS_PER_TOKEN = 2 * 2084044800  # 2B shape: 69,468,160 ternary weights per layer x 30 layers, 2 ops each
+
+
+def prefill_c3(weights, backend, cfg, seed):
+    """C3 ragged prefill: 64 seeded prompts of lengths U[32, 2048] through
+    bitnet_cuda_prefill, packed into steps of <= 1024 tokens (a prompt may
+    continue in the next step), bf16 paged KV. One untimed pass, then one
+    timed pass on a fresh cache; host token ids in, next ids out."""
+    import torch
+
+    from bitnetrs_b200 import KV_BF16, BitNetModel, synth
+
+    lens = synth.uniform_u32(seed, 21, PREFILL_SEQS, PREFILL_LO, PREFILL_HI).astype(np.int64)
+    prompts = [synth.uniform_u32(seed, 100 + s, int(n), 0, cfg.vocab_size - 1) for s, n in enumerate(lens)]
+    steps, cur_s, cur_t, used = [], [], [], 0
+    for s in range(PREFILL_SEQS):
+        pos = 0
+        while pos < lens[s]:
+            take = int(min(lens[s] - pos, PREFILL_CHUNK - used))
+            cur_s.append(s)
+            cur_t.append(prompts[s][pos:pos + take])
+            pos += take
+            used += take
+            if used == PREFILL_CHUNK:
+                steps.append((cur_s, cur_t))
+                cur_s, cur_t, used = [], [], 0
+    if cur_s:
+        steps.append((cur_s, cur_t))
+    model = BitNetModel(weights, backend, max_batch_tokens=PREFILL_CHUNK)
+    pages = int(np.sum((lens + 15) // 16)) + 64
+    dt = 0.0
+    for rep_i in range(2):
+        kv = model.new_kv_cache(num_pages=pages, max_seqs=PREFILL_SEQS, kv_dtype=KV_BF16)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for seqs, toks in steps:
+            model.prefill(kv, seqs, toks)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        kv.close()
+    model.close()
+    T = int(lens.sum())
+    attn = float(np.sum(30 * 20 * 4 * 128 * lens * (lens + 1) / 2))
+    return {"value": T / dt, "unit": "tokens/s", "tokens": T, "seqs": PREFILL_SEQS,
+            "lens": f"U[{PREFILL_LO},{PREFILL_HI}] seeded", "steps": len(steps), "tokens_per_step": PREFILL_CHUNK,
+            "s": round(dt, 4),
+            # total work of each kind over the whole prefill time (not kernel rates)
+            "ternary_int8_tops_over_wall": TERNARY_OPS_PER_TOKEN * T / dt / 1e12,
+            "attention_tflops_over_wall": attn / dt / 1e12,
+            "api": "bitnet_cuda_prefill (host ids in, greedy next ids out, host-timed), reference-order "
+                   "attention, tcgen05 ternary GEMM"}
+
+
 def run_cuda(a):
     import torch
 
@@ -439,6 +495,11 @@ def run_cuda(a):
     if rank == 0 and not a.no_gemv_sweep:
         gemv_m1 = gemv_sweep(backend, dev, peak)
 
+    # ---- C3 ragged prefill (rank 0, N=1) ----
+    prefill = None
+    if rank == 0 and world == 1 and not a.no_prefill:
+        prefill = prefill_c3(weights, backend, cfg, rank_seed)
+
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -473,6 +534,7 @@ def run_cuda(a):
                      "tops": mm_ops / (mm_ms / 1e3) / 1e12 if mm_ms else None},
             "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kt.items()},
             "batch1": b1,
+            "prefill": prefill,
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": int(launches),
