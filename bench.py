@@ -520,7 +520,7 @@ def run_cuda(a):
                        "global_batch": B * world, "ctx": f"U[{CTX_LO},{a.ctx_hi}] seeded per rank",
                        "kv": "paged bf16, 16-token pages", "parallelism": f"dp{world} (replicated weights, no "
                                                                          f"collective)",
-                       "l2": "inputs larger than L2 (~44 GB of KV read per step)"},
+                       "l2": f"inputs larger than L2 ({attn_bytes * L / 1e9:.1f} GB of KV read per step)"},
             "e2e": e2e,
             "roofline": {"bound": "hbm", "kernel": attn_kernel,
                          "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
