@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """bench.py — BitNet-2B decode throughput on B200 (bitnetrs hot path).
 
-Default workload (BASELINE config "continuous-batching decode"): the 2B
+Default workload (continuous-batching decode): the 2B
 architecture with random-init weights (N(0,0.02), absmean-ternarised, packed
 in the reference format), 256 concurrent sequences per GPU whose contexts are
 seeded with lengths U[128, 4096] and N(0,1) bf16 K/V, greedy decode.  A step
@@ -463,7 +463,7 @@ def run_cuda(a):
            "h2d_bytes_per_step": int(B * 4 + B * 8), "d2h_bytes_per_step": int(B * 4),
            "api": "bitnet_cuda_decode_step (host token ids in, greedy next ids out)", "steps": E2E_STEPS}
 
-    # ---- batch-1 decode (BASELINE's batch-1 number), same model ----
+    # ---- batch-1 decode, same model ----
     b1 = None
     s1 = B  # spare sequence slot
     kv.fill_random(s1, 128, rank_seed + 7)

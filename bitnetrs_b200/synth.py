@@ -74,7 +74,7 @@ def kv_normal(seed: int, seq: int, cfg: ModelConfig, n: int):
 
 
 def random_model(cfg: ModelConfig, seed: int = 0, std: float = 0.02, norm_gain: float = 1.0) -> ModelWeights:
-    """Random-init model with the reference's weight formats (std 0.02, norm gains 1.0)."""
+    """Random-init model with the reference's weight formats (weights N(0, 0.02), norm gains 1.0)."""
     H, F, V, qd, kvd = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size, cfg.q_dim(), cfg.kv_dim()
     layers = []
     for l in range(cfg.num_hidden_layers):

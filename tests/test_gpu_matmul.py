@@ -1,5 +1,5 @@
-"""Op sweep of the ternary matmul (BASELINE config "ternary matmul op sweep"):
-the 2B layer shapes at M in {1, 8, 64, 512} plus edge sizes, through the
+"""Op sweep of the ternary matmul: the 2B layer shapes at M from 1 to 512
+plus edge sizes, through the
 device-resident C-ABI entry points.  Int8 activations and int32
 accumulators must be bit-exact; f32 outputs bit-exact against the oracle's
 ternary_gemv_quantised applied per row."""

@@ -351,7 +351,7 @@ def _raise_invalid_config(backend):
 
 @pytest.mark.parametrize("kv_dtype", [KV_F32, KV_BF16], ids=["f32kv", "bf16kv"])
 def test_2b_greedy_decode_token_identical(cuda_backend, kv_dtype):
-    """2B architecture, random init, 128-token seeded
+    """The 2B architecture, random init, 128-token seeded
     prompt, 128 greedy tokens at batch 1.  The oracle decodes greedily; the
     GPU is fed the same tokens (teacher forcing) so every step's logits are
     compared on identical inputs: logits within the north-star 1e-2 relative
