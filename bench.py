@@ -296,29 +296,17 @@ TERNARY_OPS_PER_TOKEN = 2 * 2084044800  # 2B shape: 69,468,160 ternary weights p
 
 def prefill_c3(weights, backend, cfg, seed):
     """C3 ragged prefill: 64 seeded prompts of lengths U[32, 2048] through
-    bitnet_cuda_prefill, packed into steps of <= 1024 tokens (a prompt may
-    continue in the next step), bf16 paged KV. One untimed pass, then one
-    timed pass on a fresh cache; host token ids in, next ids out."""
+    BitNetModel.prefill_packed (bitnet_cuda_prefill in steps of <= 1024 tokens,
+    a prompt may continue in the next step), bf16 paged KV. One untimed pass,
+    then one timed pass on a fresh cache; host token ids in, next ids out."""
     import torch
 
     from bitnetrs_b200 import KV_BF16, BitNetModel, synth
+    from bitnetrs_b200.batching import pack_steps
 
     lens = synth.uniform_u32(seed, 21, PREFILL_SEQS, PREFILL_LO, PREFILL_HI).astype(np.int64)
     prompts = [synth.uniform_u32(seed, 100 + s, int(n), 0, cfg.vocab_size - 1) for s, n in enumerate(lens)]
-    steps, cur_s, cur_t, used = [], [], [], 0
-    for s in range(PREFILL_SEQS):
-        pos = 0
-        while pos < lens[s]:
-            take = int(min(lens[s] - pos, PREFILL_CHUNK - used))
-            cur_s.append(s)
-            cur_t.append(prompts[s][pos:pos + take])
-            pos += take
-            used += take
-            if used == PREFILL_CHUNK:
-                steps.append((cur_s, cur_t))
-                cur_s, cur_t, used = [], [], 0
-    if cur_s:
-        steps.append((cur_s, cur_t))
+    n_steps = len(pack_steps([int(n) for n in lens], PREFILL_CHUNK))
     model = BitNetModel(weights, backend, max_batch_tokens=PREFILL_CHUNK)
     pages = int(np.sum((lens + 15) // 16)) + 64
     dt = 0.0
@@ -326,8 +314,7 @@ def prefill_c3(weights, backend, cfg, seed):
         kv = model.new_kv_cache(num_pages=pages, max_seqs=PREFILL_SEQS, kv_dtype=KV_BF16)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        for seqs, toks in steps:
-            model.prefill(kv, seqs, toks)
+        model.prefill_packed(kv, list(range(PREFILL_SEQS)), prompts)
         torch.cuda.synchronize()
         dt = time.perf_counter() - t0
         kv.close()
@@ -335,7 +322,7 @@ def prefill_c3(weights, backend, cfg, seed):
     T = int(lens.sum())
     attn = float(np.sum(30 * 20 * 4 * 128 * lens * (lens + 1) / 2))
     return {"value": T / dt, "unit": "tokens/s", "tokens": T, "seqs": PREFILL_SEQS,
-            "lens": f"U[{PREFILL_LO},{PREFILL_HI}] seeded", "steps": len(steps), "tokens_per_step": PREFILL_CHUNK,
+            "lens": f"U[{PREFILL_LO},{PREFILL_HI}] seeded", "steps": n_steps, "tokens_per_step": PREFILL_CHUNK,
             "s": round(dt, 4),
             # total work of each kind over the whole prefill time (not kernel rates)
             "ternary_int8_tops_over_wall": TERNARY_OPS_PER_TOKEN * T / dt / 1e12,

@@ -219,6 +219,30 @@ class BitNetModel:
                                             ptr(nxt)))
         return nxt, logits
 
+    def prefill_packed(self, kv: "KVCache", seq_ids, token_lists, want_logits: bool = False):
+        """Ragged prefill of any number of prompt tokens: the prompts are packed
+        into steps of at most ``max_batch_tokens`` (batching.pack_steps) and run
+        in order. Returns, per sequence, the greedy next token and (optionally)
+        the logits after its last prompt token; an empty prompt gets
+        next token 0 and zero logits."""
+        from .batching import pack_steps
+
+        seq_ids = [int(x) for x in seq_ids]
+        if len(seq_ids) != len(token_lists):
+            raise ValueError("seq_ids and token_lists must have the same length")
+        lens = [len(x) for x in token_lists]
+        nxt = np.zeros(len(seq_ids), dtype=np.uint32)
+        logits = np.zeros((len(seq_ids), self.config.vocab_size), dtype=np.float32) if want_logits else None
+        for step in pack_steps(lens, self.max_batch_tokens):
+            n, lg = self.prefill(kv, [seq_ids[i] for i, _, _ in step],
+                                 [np.asarray(token_lists[i])[a:a + c] for i, a, c in step], want_logits)
+            for j, (i, a, c) in enumerate(step):
+                if a + c == lens[i]:  # the prompt's last chunk
+                    nxt[i] = n[j]
+                    if want_logits:
+                        logits[i] = lg[j]
+        return nxt, logits
+
     def check(self) -> None:
         check(self._lib.bitnet_cuda_model_check(self._h))
 

@@ -113,6 +113,28 @@ def test_long_prompt_chunked_prefill(cuda_backend, small):
     close_logits(m.forward(toks, 0, kv), om.forward(okv, toks, 0))
 
 
+def test_prefill_packed_long_ragged(cuda_backend, small):
+    """Prompts longer than the model's token capacity, packed into steps (a
+    prompt continues in the next step): each sequence's logits and greedy
+    token match the oracle's forward over the whole prompt."""
+    cfg, w = small
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=32)
+    lens = [50, 7, 32, 0, 70]
+    seqs = [0, 2, 3, 4, 5]
+    prompts = [synth.uniform_u32(60 + i, 2, n, 0, cfg.vocab_size - 1).tolist() if n else [] for i, n in enumerate(lens)]
+    kv = m.new_kv_cache(num_pages=64, max_seqs=6)
+    nxt, logits = m.prefill_packed(kv, seqs, prompts, want_logits=True)
+    om = O.OracleModel(w)
+    for i, s in enumerate(seqs):
+        assert kv.len(s) == lens[i]
+        if not lens[i]:
+            assert nxt[i] == 0
+            continue
+        r = om.forward(om.kv(cfg.max_position_embeddings), prompts[i], 0)
+        close_logits(logits[i], r)
+        assert nxt[i] == O.lib().orc_greedy_argmax(O.p(r), r.size)
+
+
 @pytest.mark.parametrize("kv_dtype", [KV_F32, KV_BF16])
 def test_batched_decode_and_ragged_prefill(cuda_backend, small, kv_dtype):
     cfg, w = small
