@@ -91,6 +91,9 @@ _CUDA_SIGS = {
     "bitnet_cuda_ternary_matmul_device": (i32, [vp, vp, vp, sz, vp, vp, sz, vp, vp, vp]),
     "bitnet_cuda_model_create": (i32, [vp, C.POINTER(Config), C.POINTER(Weights), u32, C.POINTER(vp)]),
     "bitnet_cuda_model_destroy": (None, [vp]),
+    "bitnet_cuda_tp_unique_id": (i32, [vp, sz]),
+    "bitnet_cuda_model_create_tp": (i32, [vp, C.POINTER(Config), C.POINTER(Weights), u32, u32, u32, vp, sz,
+                                          C.POINTER(vp)]),
     "bitnet_cuda_kv_create": (i32, [vp, u32, u32, i32, C.POINTER(vp)]),
     "bitnet_cuda_kv_destroy": (None, [vp]),
     "bitnet_cuda_kv_seq_reset": (i32, [vp, u32]),

@@ -14,6 +14,7 @@
 #include <cstring>
 
 #include "internal.h"
+#include "tp.cuh"
 
 using namespace bitnet;
 
@@ -74,6 +75,15 @@ struct bitnet_cuda_model {
   bool timing = false;
   const Graph* last_timed = nullptr;
   std::vector<std::tuple<int, cudaEvent_t, cudaEvent_t>>* marks = nullptr;  // set while capturing a timed graph
+  // tensor parallelism (bitnet_cuda_model_create_tp): nh, nkv, qd, kvd and F
+  // above are this rank's share; qd_all and F_all the full widths
+  bool tp = false;
+  int tp_rank = 0, tp_world = 1, qd_all = 0, F_all = 0;
+  const NcclApi* nc = nullptr;
+  ncclComm_t comm = nullptr;
+  ncclResult_t nccl_rc = ncclSuccess;  // first failed collective since the last check
+  float *tp_gath = nullptr, *tp_full = nullptr;  // [world][T][C] all-gather, [T][world*C] full rows
+  int32_t *tp_acc = nullptr, *tp_rowsum = nullptr;  // [T][H] partial then total accumulators; slice row sums
 
   template <class T>
   int alloc(T** p, size_t n) {
@@ -228,6 +238,35 @@ void timed(bitnet_cuda_model* m, int cls, cudaStream_t st, F launch) {
   m->marks->emplace_back(cls, a, b);
 }
 
+void nccl_note(bitnet_cuda_model* m, ncclResult_t r) {
+  if (r != ncclSuccess && m->nccl_rc == ncclSuccess) m->nccl_rc = r;
+}
+
+// Tensor parallelism: all-gather this rank's [T][C] chunk (already in its
+// slot of tp_gath) and lay the result out as full rows [T][world*C] in tp_full.
+void tp_gather_rows(bitnet_cuda_model* m, int T, int C, cudaStream_t st) {
+  const size_t cnt = (size_t)T * C;
+  nccl_note(m, m->nc->all_gather(m->tp_gath + (size_t)m->tp_rank * cnt, m->tp_gath, cnt, ncclFloat32, m->comm, st));
+  launch_tp_unchunk(m->tp_gath, m->tp_world, T, C, m->tp_full, st);
+}
+
+// Tensor parallelism, row-split projection (o_proj, down_proj): this rank's K
+// input columns of W against its slice of the quantised full rows, the int32
+// accumulators summed over ranks (exact), then the reference epilogue with
+// the residual add into h on every rank.
+void tp_row_split(bitnet_cuda_model* m, const uint32_t* W, int K, float ws, int T, cudaStream_t st) {
+  const int H = m->H;
+  const int8_t* xs = m->xq + (size_t)m->tp_rank * K;
+  launch_row_sum(xs, m->ldq, T, K, m->tp_rowsum, st);
+  Segments s;
+  s.end[0] = s.end[1] = s.end[2] = H;
+  s.scale[0] = s.scale[1] = s.scale[2] = ws;
+  launch_ternary_matmul(W, H, K, xs, m->ldq, m->amax, m->tp_rowsum, T, s, Epi::Store, m->qrot, H, m->tp_acc, st,
+                        m->status);
+  nccl_note(m, m->nc->all_reduce(m->tp_acc, m->tp_acc, (size_t)T * H, ncclInt32, ncclSum, m->comm, st));
+  launch_acc_epilogue(m->tp_acc, T, H, ws, m->amax, Epi::Residual, m->h, H, st);
+}
+
 // Run the transformer over T tokens whose metadata (tokens, tok_pos, tok_seq,
 // last_row) is already on the device.  n_out rows of final hidden state
 // (selected by last_row) go through final norm, lm_head and argmax.
@@ -260,34 +299,46 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
       launch_rope_kv_store(m->qkv, nqkv, T, m->nh, m->nkv, m->hd, m->rope_cos, m->rope_sin, m->tok_pos, m->tok_seq,
                            kv->d_table, kv->g, l, m->qrot, st);
     });
+    // a tensor-parallel rank writes its heads straight into its all-gather slot
+    float* attn_out = m->tp ? m->tp_gath + (size_t)m->tp_rank * T * qd : m->attn;
     timed(m, kAttn, st, [&] {
       if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx))
         launch_paged_attention_exact3(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, kv->tmap, l,
-                                      max_ctx, m->attn, m->ctx->exp_table, m->status, st);
+                                      max_ctx, attn_out, m->ctx->exp_table, m->status, st);
       else if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx))
         launch_paged_attention_exact2(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx,
-                                      m->attn, m->ctx->exp_table, st);
+                                      attn_out, m->ctx->exp_table, st);
       else if (use_exact_attention(m, T))
         launch_paged_attention_exact(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx,
-                                     m->attn, m->partial.as<float>(), exact_scores_in_smem(m, max_ctx),
+                                     attn_out, m->partial.as<float>(), exact_scores_in_smem(m, max_ctx),
                                      m->ctx->exp_table, st);
       else if (use_mma_attention(m, kv, T))
-        launch_flash_decode_mma(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, m->attn,
+        launch_flash_decode_mma(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, attn_out,
                                 m->partial.as<float>(), st);
       else
-        launch_paged_attention(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, m->attn,
+        launch_paged_attention(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, l, max_ctx, attn_out,
                                m->partial.as<float>(), m->partial.cap / 4, st);
     });
-    timed(m, kNormQuant, st, [&] {
-      launch_norm_quant(m->attn, nullptr, qd, Lw.attn_sub_norm, qd, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status,
-                        T, st);
-    });
-    Segments so;
-    so.end[0] = so.end[1] = so.end[2] = H;
-    so.scale[0] = so.scale[1] = so.scale[2] = Lw.so;
-    timed(m, kMatmul, st, [&] {
-      launch_ternary_matmul(Lw.wo, H, qd, m->xq, m->ldq, m->amax, m->rowsum, T, so, Epi::Residual, m->h, H, nullptr, st, m->status);
-    });
+    if (m->tp) {
+      timed(m, kOther, st, [&] { tp_gather_rows(m, T, qd, st); });
+      timed(m, kNormQuant, st, [&] {
+        launch_norm_quant(m->tp_full, nullptr, m->qd_all, Lw.attn_sub_norm, m->qd_all, eps, m->xq, m->ldq, m->amax,
+                          m->rowsum, m->status, T, st);
+      });
+      timed(m, kMatmul, st, [&] { tp_row_split(m, Lw.wo, qd, Lw.so, T, st); });
+    } else {
+      timed(m, kNormQuant, st, [&] {
+        launch_norm_quant(m->attn, nullptr, qd, Lw.attn_sub_norm, qd, eps, m->xq, m->ldq, m->amax, m->rowsum,
+                          m->status, T, st);
+      });
+      Segments so;
+      so.end[0] = so.end[1] = so.end[2] = H;
+      so.scale[0] = so.scale[1] = so.scale[2] = Lw.so;
+      timed(m, kMatmul, st, [&] {
+        launch_ternary_matmul(Lw.wo, H, qd, m->xq, m->ldq, m->amax, m->rowsum, T, so, Epi::Residual, m->h, H, nullptr,
+                              st, m->status);
+      });
+    }
     // FFN block
     timed(m, kNormQuant, st, [&] {
       launch_norm_quant(m->h, nullptr, H, Lw.ffn_norm, H, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status, T, st);
@@ -302,17 +353,29 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
       launch_ternary_matmul(Lw.wgu, 2 * F, H, m->xq, m->ldq, m->amax, m->rowsum, T, sgu, Epi::Store, m->gu, 2 * F,
                             nullptr, st, m->status);
     });
-    timed(m, kNormQuant, st, [&] {
-      launch_norm_quant(m->gu, m->gu + F, 2 * F, Lw.ffn_sub_norm, F, eps, m->xq, m->ldq, m->amax, m->rowsum, m->status,
-                        T, st);
-    });
-    Segments sd;
-    sd.end[0] = sd.end[1] = sd.end[2] = H;
-    sd.scale[0] = sd.scale[1] = sd.scale[2] = Lw.sd;
-    timed(m, kMatmul, st, [&] {
-      launch_ternary_matmul(Lw.wdown, H, F, m->xq, m->ldq, m->amax, m->rowsum, T, sd, Epi::Residual, m->h, H, nullptr,
-                            st, m->status);
-    });
+    if (m->tp) {
+      timed(m, kOther, st, [&] {
+        launch_tp_gate_rows(m->gu, T, F, m->tp_gath + (size_t)m->tp_rank * T * F, st);
+        tp_gather_rows(m, T, F, st);
+      });
+      timed(m, kNormQuant, st, [&] {
+        launch_norm_quant(m->tp_full, nullptr, m->F_all, Lw.ffn_sub_norm, m->F_all, eps, m->xq, m->ldq, m->amax,
+                          m->rowsum, m->status, T, st);
+      });
+      timed(m, kMatmul, st, [&] { tp_row_split(m, Lw.wdown, F, Lw.sd, T, st); });
+    } else {
+      timed(m, kNormQuant, st, [&] {
+        launch_norm_quant(m->gu, m->gu + F, 2 * F, Lw.ffn_sub_norm, F, eps, m->xq, m->ldq, m->amax, m->rowsum,
+                          m->status, T, st);
+      });
+      Segments sd;
+      sd.end[0] = sd.end[1] = sd.end[2] = H;
+      sd.scale[0] = sd.scale[1] = sd.scale[2] = Lw.sd;
+      timed(m, kMatmul, st, [&] {
+        launch_ternary_matmul(Lw.wdown, H, F, m->xq, m->ldq, m->amax, m->rowsum, T, sd, Epi::Residual, m->h, H,
+                              nullptr, st, m->status);
+      });
+    }
   }
   // final norm on the selected rows, lm_head, greedy argmax
   timed(m, kOther, st, [&] {
@@ -349,6 +412,11 @@ int check_status(bitnet_cuda_model* m) {
   if (s) {
     BN_CUDA(cudaMemsetAsync(m->status, 0, 4, m->ctx->stream));
     BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  }
+  if (m->nccl_rc != ncclSuccess) {
+    ncclResult_t r = m->nccl_rc;
+    m->nccl_rc = ncclSuccess;
+    return backend_error(std::string("NCCL collective failed: ") + m->nc->error_string(r));
   }
   if (s & kStatusWaitTimeout) return backend_error("a device-side wait timed out (attention pipeline)");
   if (s & kStatusBadContext) return backend_error("a token's context exceeds the attention kernel's capacity");
@@ -437,6 +505,7 @@ static void model_release(bitnet_cuda_model* m) {
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
   drop_graphs(m);
+  if (m->comm) m->nc->comm_destroy(m->comm);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_meta) cudaFreeHost(m->h_meta);
   if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -445,39 +514,88 @@ static void model_release(bitnet_cuda_model* m) {
   ctx_release(c);
 }
 
-extern "C" {
+namespace {
 
-int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const bitnet_cuda_weights* w,
-                             uint32_t max_batch_tokens, bitnet_cuda_model** out) {
+// Uploads the share of rank `rank` of `world`; without an NCCL id the whole
+// model on one device with no collectives.
+int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const bitnet_cuda_weights* w,
+                      uint32_t max_batch_tokens, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
+                      bitnet_cuda_model** out) {
   if (!out || !cfg || !w || !ctx) return shape_error("non-null arguments", "null");
   *out = nullptr;
   BN_TRY(validate_config(*cfg));
   if (max_batch_tokens == 0) return shape_error("max_batch_tokens > 0", "0");
   if (!w->layers) return shape_error("non-null layers", "null");
+  const bool tp = nccl_id != nullptr;
+  const NcclApi* nc = nullptr;
+  if (tp) {
+    const uint32_t nh = cfg->num_attention_heads, nkv = cfg->num_key_value_heads;
+    const size_t qd_all = (size_t)(cfg->hidden_size / nh) * nh;
+    if (world == 0 || rank >= world) return config_error("tensor-parallel rank must be < world (world > 0)");
+    if (nh % world != 0 || nkv % world != 0)
+      return config_error("num_attention_heads (" + sz(nh) + ") and num_key_value_heads (" + sz(nkv) +
+                          ") must be divisible by the tensor-parallel world (" + sz(world) + ")");
+    if (cfg->intermediate_size % world != 0 || (qd_all / world) % 64 != 0 || (cfg->intermediate_size / world) % 64 != 0)
+      return config_error("per-rank attention width (" + sz(qd_all / world) + ") and intermediate slice (" +
+                          sz(cfg->intermediate_size / world) + ") must be multiples of 64");
+    std::string why;
+    nc = nccl_api(&why);
+    if (!nc) return backend_error("tensor parallelism needs NCCL: " + why);
+  }
   std::lock_guard<std::mutex> lk(ctx->mu);
   cudaSetDevice(ctx->device);
   auto* m = new bitnet_cuda_model();
   m->ctx = ctx;
   ctx_retain(ctx);
   m->cfg = *cfg;
+  const int G = tp ? (int)world : 1, rk = tp ? (int)rank : 0;
+  m->tp = tp;
+  m->tp_rank = rk;
+  m->tp_world = G;
+  m->nc = nc;
   m->H = (int)cfg->hidden_size;
-  m->nh = (int)cfg->num_attention_heads;
-  m->nkv = (int)cfg->num_key_value_heads;
-  m->hd = m->H / m->nh;
+  m->hd = m->H / (int)cfg->num_attention_heads;
+  m->nh = (int)cfg->num_attention_heads / G;
+  m->nkv = (int)cfg->num_key_value_heads / G;
   m->qd = m->nh * m->hd;
   m->kvd = m->nkv * m->hd;
-  m->F = (int)cfg->intermediate_size;
+  m->qd_all = m->qd * G;
+  m->F_all = (int)cfg->intermediate_size;
+  m->F = m->F_all / G;
   m->V = (int)cfg->vocab_size;
   m->L = (int)cfg->num_hidden_layers;
   m->Tmax = (int)max_batch_tokens;
-  m->ldq = (int)std::max({padded_cols(m->H), padded_cols(m->qd), padded_cols(m->F)});
+  m->ldq = (int)std::max({padded_cols(m->H), padded_cols(m->qd_all), padded_cols(m->F_all)});
   auto fail = [&](int rc) {
     model_release(m);
     return rc;
   };
   int rc;
+  if (tp) {
+    // collective: every rank rendezvouses here before any upload
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof id);
+    ncclResult_t r = nc->comm_init_rank(&m->comm, G, id, rk);
+    if (r != ncclSuccess) {
+      m->comm = nullptr;
+      return fail(backend_error(std::string("ncclCommInitRank: ") + nc->error_string(r)));
+    }
+  }
   DevBuf tmp;
   const int H = m->H, qd = m->qd, kvd = m->kvd, F = m->F;
+  const size_t pcH = ((size_t)H + 3) / 4;
+  // input columns [rk*k, (rk+1)*k) of a [H][K] reference-format tensor, k % 4 == 0
+  std::vector<uint8_t> cols;
+  auto col_slice = [&](const uint8_t* src, int K, int k) -> const uint8_t* {
+    if (!src || G == 1) return src;
+    const size_t pc = ((size_t)K + 3) / 4, pk = (size_t)k / 4;
+    cols.resize((size_t)H * pk);
+    for (int i = 0; i < H; ++i) std::memcpy(&cols[(size_t)i * pk], src + (size_t)i * pc + (size_t)rk * pk, pk);
+    return cols.data();
+  };
+  auto row_slice = [&](const uint8_t* src, int rows) -> const uint8_t* {
+    return src ? src + (size_t)rk * rows * pcH : src;
+  };
   for (int l = 0; l < m->L; ++l) {
     const bitnet_cuda_layer_weights& s = w->layers[l];
     Layer Lw;
@@ -494,17 +612,19 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
     if ((rc = m->alloc(&Lw.wo, (size_t)H * words_per_row(qd)))) return fail(rc);
     if ((rc = m->alloc(&Lw.wgu, (size_t)2 * F * words_per_row(H)))) return fail(rc);
     if ((rc = m->alloc(&Lw.wdown, (size_t)H * words_per_row(F)))) return fail(rc);
-    if ((rc = put_ternary(m, s.q_proj, qd, H, Lw.wqkv, 0, tmp))) return fail(rc);
-    if ((rc = put_ternary(m, s.k_proj, kvd, H, Lw.wqkv, qd, tmp))) return fail(rc);
-    if ((rc = put_ternary(m, s.v_proj, kvd, H, Lw.wqkv, qd + kvd, tmp))) return fail(rc);
-    if ((rc = put_ternary(m, s.o_proj, H, qd, Lw.wo, 0, tmp))) return fail(rc);
-    if ((rc = put_ternary(m, s.gate_proj, F, H, Lw.wgu, 0, tmp))) return fail(rc);
-    if ((rc = put_ternary(m, s.up_proj, F, H, Lw.wgu, F, tmp))) return fail(rc);
-    if ((rc = put_ternary(m, s.down_proj, H, F, Lw.wdown, 0, tmp))) return fail(rc);
+    // column-split projections keep this rank's output rows; row-split ones
+    // (o, down) its input columns; the sub-norms act on full rows
+    if ((rc = put_ternary(m, row_slice(s.q_proj, qd), qd, H, Lw.wqkv, 0, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, row_slice(s.k_proj, kvd), kvd, H, Lw.wqkv, qd, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, row_slice(s.v_proj, kvd), kvd, H, Lw.wqkv, qd + kvd, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, col_slice(s.o_proj, m->qd_all, qd), H, qd, Lw.wo, 0, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, row_slice(s.gate_proj, F), F, H, Lw.wgu, 0, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, row_slice(s.up_proj, F), F, H, Lw.wgu, F, tmp))) return fail(rc);
+    if ((rc = put_ternary(m, col_slice(s.down_proj, m->F_all, F), H, F, Lw.wdown, 0, tmp))) return fail(rc);
     if ((rc = put(m, &Lw.attn_norm, s.attention_norm, H))) return fail(rc);
-    if ((rc = put(m, &Lw.attn_sub_norm, s.attn_sub_norm, qd))) return fail(rc);
+    if ((rc = put(m, &Lw.attn_sub_norm, s.attn_sub_norm, m->qd_all))) return fail(rc);
     if ((rc = put(m, &Lw.ffn_norm, s.ffn_norm, H))) return fail(rc);
-    if ((rc = put(m, &Lw.ffn_sub_norm, s.ffn_sub_norm, F))) return fail(rc);
+    if ((rc = put(m, &Lw.ffn_sub_norm, s.ffn_sub_norm, m->F_all))) return fail(rc);
     m->layers.push_back(Lw);
   }
   const size_t V = m->V;
@@ -561,6 +681,13 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
   if ((rc = m->alloc(&m->tok_seq, T))) return fail(rc);
   if ((rc = m->alloc(&m->last_row, T))) return fail(rc);
   if ((rc = m->alloc(&m->status, 16))) return fail(rc);
+  if (tp) {
+    const size_t wide = (size_t)std::max(m->qd_all, m->F_all);
+    if ((rc = m->alloc(&m->tp_gath, T * wide))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_full, T * wide))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_acc, T * H))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_rowsum, T))) return fail(rc);
+  }
   cudaError_t e = cudaMallocHost(&m->h_meta, 3 * T * sizeof(int32_t));
   if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
   e = cudaMallocHost(&m->h_tokens, T * sizeof(uint32_t));
@@ -571,6 +698,25 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg
   if (e != cudaSuccess) return fail(cuda_error(e, "model upload"));
   *out = m;
   return BITNET_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const bitnet_cuda_weights* w,
+                             uint32_t max_batch_tokens, bitnet_cuda_model** out) {
+  return model_create_impl(ctx, cfg, w, max_batch_tokens, 0, 1, nullptr, out);
+}
+
+int bitnet_cuda_model_create_tp(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const bitnet_cuda_weights* w,
+                                uint32_t max_batch_tokens, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
+                                size_t id_len, bitnet_cuda_model** out) {
+  if (out) *out = nullptr;
+  if (!nccl_id) return shape_error("non-null NCCL id", "null");
+  if (id_len < sizeof(ncclUniqueId))
+    return shape_error("id_len >= " + sz(sizeof(ncclUniqueId)), sz(id_len));
+  return model_create_impl(ctx, cfg, w, max_batch_tokens, rank, world, nccl_id, out);
 }
 
 void bitnet_cuda_model_destroy(bitnet_cuda_model* m) {
@@ -796,6 +942,13 @@ static int decode_graph(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t batch, 
     BN_CUDA(cudaMemcpyAsync(m->tokens, m->h_tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st));
   } else {
     BN_CUDA(cudaMemcpyAsync(m->tokens, src, (size_t)T * 4, cudaMemcpyDeviceToDevice, st));
+  }
+  if (m->tp) {
+    // tensor-parallel steps launch eagerly: their NCCL calls are not captured
+    run_forward(m, kv, T, T, max_ctx, st);
+    BN_CUDA(cudaGetLastError());
+    for (size_t i = 0; i < batch; ++i) kv->seq_len[seq_ids[i]] += 1;
+    return BITNET_OK;
   }
   auto key = std::make_tuple((void*)kv, T, m->timing ? 1 : 0);
   auto it = m->graphs.find(key);

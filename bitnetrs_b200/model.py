@@ -64,6 +64,13 @@ def bitnet_2b_config() -> ModelConfig:
     return ModelConfig(128_256, 2560, 30, 20, 5, 6912, 4096, 500_000.0, 1e-5)
 
 
+def scaled_model_config() -> ModelConfig:
+    """The larger shape served tensor-parallel: hidden 4096, 32 layers, 32
+    query / 8 KV heads of 128, intermediate 14336, the 2B vocabulary, RoPE
+    theta and eps (the 2B family's layer structure at Llama-3-8B widths)."""
+    return ModelConfig(128_256, 4096, 32, 32, 8, 14336, 4096, 500_000.0, 1e-5)
+
+
 def tiny_config() -> ModelConfig:
     """The reference's unit-test model (crates/bitnet-model/src/lib.rs:1267-1279)."""
     return ModelConfig(16, 8, 2, 2, 1, 16, 32, 10000.0, 1e-5)
@@ -144,16 +151,27 @@ def _check_weights(w: ModelWeights) -> None:
 class BitNetModel:
     """Weights resident on one GPU; forward passes run entirely on the device."""
 
-    def __init__(self, weights: ModelWeights, backend: Optional[CudaBackend] = None, max_batch_tokens: int = 4096):
+    def __init__(self, weights: ModelWeights, backend: Optional[CudaBackend] = None, max_batch_tokens: int = 4096,
+                 tp=None):
+        """`tp` (a :class:`bitnetrs_b200.tp.TensorParallel`) makes this a
+        tensor-parallel shard: `weights` is the full model, the device keeps
+        this rank's share, and every rank must run the same calls together."""
         _check_weights(weights)
         self.backend = backend if backend is not None else CudaBackend(0)
         self.config = weights.config
+        self.tp = tp
         self._lib = N.cuda_lib()
         cw, keep = _c_weights(weights)
         cfg = weights.config.to_c()
         h = C.c_void_p()
-        check(self._lib.bitnet_cuda_model_create(self.backend.handle, C.byref(cfg), C.byref(cw), max_batch_tokens,
-                                                 C.byref(h)))
+        if tp is None:
+            check(self._lib.bitnet_cuda_model_create(self.backend.handle, C.byref(cfg), C.byref(cw),
+                                                     max_batch_tokens, C.byref(h)))
+        else:
+            uid = (C.c_uint8 * len(tp.unique_id)).from_buffer_copy(tp.unique_id)
+            check(self._lib.bitnet_cuda_model_create_tp(self.backend.handle, C.byref(cfg), C.byref(cw),
+                                                        max_batch_tokens, tp.rank, tp.world, uid, len(tp.unique_id),
+                                                        C.byref(h)))
         self._h = h
         self.max_batch_tokens = max_batch_tokens
 

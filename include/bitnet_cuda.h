@@ -245,6 +245,34 @@ int bitnet_cuda_model_create(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* con
                              uint32_t max_batch_tokens, bitnet_cuda_model** out);
 void bitnet_cuda_model_destroy(bitnet_cuda_model* model);
 
+/* Tensor parallelism for models too large for one device (no counterpart in
+ * the reference, which runs on one device).  Rank `rank` of `world` keeps the
+ * q/k/v rows of its num_attention_heads/world query heads and
+ * num_key_value_heads/world KV heads, the gate/up rows of its
+ * intermediate_size/world slice, and the matching input columns of o_proj and
+ * down_proj; per-tensor scales stay those of the full tensors.  Every layer
+ * all-gathers the attention output and the gated FFN activation, so that both
+ * sub-norms and their int8 quantisation run over the full row in the
+ * reference's order, and all-reduces the int32 accumulators of o_proj and
+ * down_proj (exact), so every rank's hidden state is bit-identical to the
+ * single-device model's.  Collectives run over NCCL, loaded at run time
+ * (the process's libnccl.so.2, or BITNET_NCCL_LIBRARY).
+ *
+ * bitnet_cuda_tp_unique_id writes BITNET_TP_ID_BYTES bytes on one rank; every
+ * rank then calls bitnet_cuda_model_create_tp with those bytes and the FULL
+ * host weights (collective: all ranks call it together), and every later
+ * forward, prefill and decode step on all ranks together with the same
+ * batch.  Tensor-parallel steps launch without CUDA-graph capture.
+ * Requirements:
+ * num_attention_heads and num_key_value_heads divisible by world, and
+ * (hidden_size/num_attention_heads)*num_attention_heads/world and
+ * intermediate_size/world multiples of 64 (ConfigError otherwise). */
+#define BITNET_TP_ID_BYTES 128
+int bitnet_cuda_tp_unique_id(uint8_t* id, size_t id_len);
+int bitnet_cuda_model_create_tp(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* config, const bitnet_cuda_weights* w,
+                                uint32_t max_batch_tokens, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
+                                size_t id_len, bitnet_cuda_model** out);
+
 #define BITNET_KV_F32 0  /* the reference KVCache element type (model/src/lib.rs:118-169) */
 #define BITNET_KV_BF16 1 /* paged bf16 cache */
 
