@@ -91,6 +91,9 @@ _CUDA_SIGS = {
     "bitnet_cuda_ternary_matmul_device": (i32, [vp, vp, vp, sz, vp, vp, sz, vp, vp, vp]),
     "bitnet_cuda_model_create": (i32, [vp, C.POINTER(Config), C.POINTER(Weights), u32, C.POINTER(vp)]),
     "bitnet_cuda_model_destroy": (None, [vp]),
+    "bitnet_cuda_decode_hf_packed": (i32, [vp, sz, sz, sz, f32, vp, sz]),
+    "bitnet_cuda_absmean_ternary": (i32, [vp, sz, sz, vp, sz, C.POINTER(f32)]),
+    "bitnet_cuda_lm_head_i8_table": (i32, [vp, sz, sz, vp, vp]),
     "bitnet_cuda_tp_unique_id": (i32, [vp, sz]),
     "bitnet_cuda_model_create_tp": (i32, [vp, C.POINTER(Config), C.POINTER(Weights), u32, u32, u32, vp, sz,
                                           C.POINTER(vp)]),

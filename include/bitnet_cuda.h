@@ -263,15 +263,44 @@ void bitnet_cuda_model_destroy(bitnet_cuda_model* model);
  * host weights (collective: all ranks call it together), and every later
  * forward, prefill and decode step on all ranks together with the same
  * batch.  Tensor-parallel steps launch without CUDA-graph capture.
- * Requirements:
- * num_attention_heads and num_key_value_heads divisible by world, and
+ * Requirements: num_attention_heads and num_key_value_heads divisible by
+ * world, and
  * (hidden_size/num_attention_heads)*num_attention_heads/world and
- * intermediate_size/world multiples of 64 (ConfigError otherwise). */
+ * intermediate_size/world multiples of 64 (InvalidConfig otherwise). */
 #define BITNET_TP_ID_BYTES 128
 int bitnet_cuda_tp_unique_id(uint8_t* id, size_t id_len);
 int bitnet_cuda_model_create_tp(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* config, const bitnet_cuda_weights* w,
                                 uint32_t max_batch_tokens, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
                                 size_t id_len, bitnet_cuda_model** out);
+
+/* ===================================================================== */
+/* Checkpoint ingestion (host only; no context needed)                    */
+/* ===================================================================== */
+
+/* decode_packed_projection (crates/bitnet-convert/src/lib.rs:235-325): the
+ * HuggingFace packed projection [packed_rows][cols] u8 -- byte (r, c) holds at
+ * bits 2s..2s+1 the lane of logical row s*packed_rows + r, value lane - 1 --
+ * into the reference runtime rows [4*packed_rows][ceil(cols/4)]
+ * (ternary.rs:266-285) that bitnet_cuda_model_create takes.  weight_scale
+ * (the checkpoint's *_scale) is only validated: it is the tensor's scale as
+ * is.  Errors: zero sizes or short buffers (InvalidShape); a non-positive or
+ * non-finite scale, or a lane 0b11 (QuantizationError, first position in the
+ * reference's scan order). */
+int bitnet_cuda_decode_hf_packed(const uint8_t* packed, size_t packed_len, size_t packed_rows, size_t cols,
+                                 float weight_scale, uint8_t* out, size_t out_len);
+
+/* quantise_weight (crates/bitnet-weights/src/loader.rs:1037-1070) for the bf16
+ * checkpoint: absmean ternarisation (absmean.rs:71-102) of a dense f32
+ * [rows][cols] tensor into reference runtime rows; *scale receives the
+ * per-tensor scale.  Empty or non-finite input: QuantizationError. */
+int bitnet_cuda_absmean_ternary(const float* w, size_t rows, size_t cols, uint8_t* out, size_t out_len,
+                                float* scale);
+
+/* quantize_bf16_rows_to_i8 (crates/bitnet-weights/src/loader.rs:297-340): the
+ * i8 table and per-row scales of the lm_head, weight-tied to the bf16
+ * embedding [rows][row_len] (raw bits). */
+int bitnet_cuda_lm_head_i8_table(const uint16_t* embed_bf16, size_t rows, size_t row_len, int8_t* out,
+                                 float* scales);
 
 #define BITNET_KV_F32 0  /* the reference KVCache element type (model/src/lib.rs:118-169) */
 #define BITNET_KV_BF16 1 /* paged bf16 cache */

@@ -18,6 +18,7 @@
 //   crates/bitnet-cpu/src/lib.rs              CpuBackend (validation order, RoPE cache reuse)
 //   crates/bitnet-model/src/lib.rs            KVCache, BitNetModel::forward / forward_into
 //   crates/bitnet-inference/src/lib.rs        greedy sample_next_token, generate loop
+//   crates/bitnet-convert/src/lib.rs          decode_packed_projection (HF packed layout)
 //
 // Floating point: compiled with -ffp-contract=off so scalar `a*b+c` stays two
 // roundings, as in Rust; FMA appears only where the reference calls
@@ -741,6 +742,28 @@ int orc_unpack_ternary(const uint8_t* packed, size_t packed_len, size_t n, int8_
     if (bits == 3) return ERR_QUANT;
     out[i] = bits == 0 ? 1 : (bits == 1 ? 0 : -1);
   }
+  return OK;
+}
+
+int orc_decode_hf_packed(const uint8_t* packed, size_t packed_len, size_t packed_rows, size_t cols, float scale,
+                         int8_t* logical) {
+  // bitnet-convert decode_packed_projection (crates/bitnet-convert/src/lib.rs:235-325):
+  // checks in its order, then for each packed row, column and shift 0,2,4,6
+  // (shift index s) the lane of logical row s*packed_rows + r is value lane-1;
+  // lane 0b11 is an error. Output: logical i8 [4*packed_rows][cols].
+  if (packed_rows == 0 || cols == 0) return ERR_SHAPE;
+  if (!(scale > 0.0f) || !finite(scale)) return ERR_QUANT;
+  size_t logical_rows = packed_rows * 4, numel = logical_rows * cols;
+  if (packed_len < (numel + 3) / 4) return ERR_SHAPE;
+  for (size_t r = 0; r < packed_rows; ++r)
+    for (size_t c = 0; c < cols; ++c) {
+      uint8_t byte = packed[r * cols + c];
+      for (int si = 0; si < 4; ++si) {
+        int lane = (byte >> (2 * si)) & 3;
+        if (lane == 3) return ERR_QUANT;
+        logical[(si * packed_rows + r) * cols + c] = (int8_t)(lane - 1);
+      }
+    }
   return OK;
 }
 

@@ -110,6 +110,24 @@ def kats():
     add("packed_bytes_rowaligned", "crates/bitnet-core/src/quant/ternary.rs:531-538", fn="packed_bytes",
         cases=[[4, 4, 4], [4, 5, 8], [3, 3, 3]])
 
+    # ---- decode_packed_projection (crates/bitnet-convert/src/lib.rs) ----
+    # lane at bits 2s of byte (r, c) -> logical row s*packed_rows + r, value lane-1
+    add("hf_decode_expands_rows_by_four", "crates/bitnet-convert/src/lib.rs:821-853", fn="hf_decode",
+        packed=[0b01_10_01_00] * 8, packed_rows=2, cols=4, scale=2.0,
+        rows=[[-1] * 4, [-1] * 4, [0] * 4, [0] * 4, [1] * 4, [1] * 4, [0] * 4, [0] * 4])
+    # the documented error conditions (lib.rs:228-233) in the order of the checks (lib.rs:243-290)
+    add("hf_decode_zero_rows", "crates/bitnet-convert/src/lib.rs:243-245", fn="hf_decode", packed=[0] * 4,
+        packed_rows=0, cols=4, scale=1.0, error="InvalidShape")
+    add("hf_decode_zero_cols", "crates/bitnet-convert/src/lib.rs:246-248", fn="hf_decode", packed=[0] * 4,
+        packed_rows=1, cols=0, scale=1.0, error="InvalidShape")
+    add("hf_decode_bad_scale", "crates/bitnet-convert/src/lib.rs:249-253", fn="hf_decode", packed=[0x55] * 4,
+        packed_rows=1, cols=4, scale=0.0, error="QuantizationError")
+    add("hf_decode_short", "crates/bitnet-convert/src/lib.rs:262-270", fn="hf_decode", packed=[0x55] * 3,
+        packed_rows=1, cols=4, scale=1.0, error="InvalidShape")
+    add("hf_decode_lane_11", "crates/bitnet-convert/src/lib.rs:279-283", fn="hf_decode",
+        packed=[0x55, 0x55, 0x55, 0x55, 0x55, 0x55, 0x55, 0b00_11_01_01], packed_rows=2, cols=4, scale=1.0,
+        error="QuantizationError", message="(1, 3), shift 4")
+
     # ---- absmax_quantize_row (crates/bitnet-core/src/quant/absmax.rs) ----
     add("absmax_max_is_127", "crates/bitnet-core/src/quant/absmax.rs:291-300", fn="absmax", x=[0.0, 1.0, 2.0, -1.0],
         q_at={"2": 127, "3": -64}, scale=2.0 / 127.0, scale_tol=1e-7)

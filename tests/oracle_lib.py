@@ -41,6 +41,7 @@ _SIGS = {
     "orc_pack_ternary": (None, [vp, sz, vp]),
     "orc_unpack_ternary": (i32, [vp, sz, sz, vp]),
     "orc_absmean_quantize": (i32, [vp, sz, vp, C.POINTER(f32)]),
+    "orc_decode_hf_packed": (i32, [vp, sz, sz, sz, f32, vp]),
     "orc_absmax_quantize_row_into": (i32, [vp, sz, vp, sz, C.POINTER(f32)]),
     "orc_quantize_bf16_rows_to_i8": (None, [vp, sz, sz, vp, vp]),
     "orc_bf16_round": (f32, [f32]),

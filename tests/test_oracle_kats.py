@@ -43,6 +43,18 @@ def test_unpack_errors(k):
     assert err(L.orc_unpack_ternary(p(pk), pk.size, k["n"], p(out))) == k["error"]
 
 
+@pytest.mark.parametrize("k", by_fn("hf_decode"), ids=lambda k: k["name"])
+def test_hf_decode(k):
+    pk = np.array(k["packed"], dtype=np.uint8)
+    out = np.zeros(max(4 * k["packed_rows"] * k["cols"], 1), dtype=np.int8)
+    rc = L.orc_decode_hf_packed(p(pk), pk.size, k["packed_rows"], k["cols"], k["scale"], p(out))
+    if "error" in k:
+        assert err(rc) == k["error"]
+    else:
+        assert rc == 0
+        assert out.reshape(-1, k["cols"]).tolist() == k["rows"]
+
+
 def test_packed_bytes_row_aligned():
     (k,) = by_fn("packed_bytes")
     for rows, cols, expected in k["cases"]:
