@@ -17,7 +17,7 @@
 //   crates/bitnet-cpu/src/activation.rs       squared_relu / softmax
 //   crates/bitnet-cpu/src/lib.rs              CpuBackend (validation order, RoPE cache reuse)
 //   crates/bitnet-model/src/lib.rs            KVCache, BitNetModel::forward / forward_into
-//   crates/bitnet-inference/src/lib.rs        greedy sample_next_token, generate loop
+//   crates/bitnet-inference/src/lib.rs        sample_next_token (greedy and full), generate loop
 //   crates/bitnet-convert/src/lib.rs          decode_packed_projection (HF packed layout)
 //
 // Floating point: compiled with -ffp-contract=off so scalar `a*b+c` stays two
@@ -39,6 +39,7 @@
 #include <cstdint>
 #include <cstring>
 #include <functional>
+#include <limits>
 #include <mutex>
 #include <thread>
 #include <vector>
@@ -901,6 +902,79 @@ int orc_lm_head_i8(const float* h, const int8_t* w, const float* scales, float* 
 }
 
 uint32_t orc_greedy_argmax(const float* logits, size_t n) { return greedy_argmax(logits, n); }
+
+// sample_next_token (crates/bitnet-inference/src/lib.rs:236-390), in place on
+// logits like the reference: repetition penalty (divide), temperature
+// (multiply by its reciprocal when |t - 1| > 1e-6), the top_k == 1 greedy
+// shortcut, top-k (mask below the k-th largest), top-p (softmax over finite
+// logits, descending order, smallest prefix with cumulative f32 probability
+// >= p), a final softmax and one LCG step (seed + number of past tokens)
+// mapped to [0, 1) for an inverse-CDF draw in index order, argmax fallback.
+// The reference orders equal probabilities with sort_unstable (unspecified);
+// here they go in ascending index order. Logits are assumed NaN-free (the
+// forward pass rejects non-finite activations).
+uint32_t orc_sample_next_token(float* logits, size_t vocab, float temperature, float top_p, size_t top_k,
+                               float repetition_penalty, uint64_t seed, const uint32_t* past, size_t n_past) {
+  if (vocab == 0) return 0;
+  const float ninf = -std::numeric_limits<float>::infinity();
+  if (repetition_penalty != 1.0f)
+    for (size_t i = 0; i < n_past; ++i)
+      if (past[i] < vocab) logits[past[i]] /= repetition_penalty;
+  if (std::fabs(temperature - 1.0f) > 1e-6f) {
+    const float inv = 1.0f / temperature;
+    for (size_t i = 0; i < vocab; ++i) logits[i] *= inv;
+  }
+  if (top_k == 1) return greedy_argmax(logits, vocab);
+  if (top_k > 0 && top_k < vocab) {
+    std::vector<float> sorted(logits, logits + vocab);
+    std::nth_element(sorted.begin(), sorted.begin() + (top_k - 1), sorted.end(), std::greater<float>());
+    const float thr = sorted[top_k - 1];
+    for (size_t i = 0; i < vocab; ++i)
+      if (logits[i] < thr) logits[i] = ninf;
+  }
+  auto softmax_finite = [&](std::vector<float>& pr) {
+    float mx = ninf;
+    for (size_t i = 0; i < vocab; ++i)
+      if (std::isfinite(logits[i])) mx = rust_max(mx, logits[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < vocab; ++i) {
+      pr[i] = std::isfinite(logits[i]) ? std::exp(logits[i] - mx) : 0.0f;
+      sum += pr[i];
+    }
+    const float inv = sum > 0.0f ? 1.0f / sum : 1.0f;
+    for (size_t i = 0; i < vocab; ++i) pr[i] *= inv;
+  };
+  std::vector<float> pr(vocab);
+  if (top_p < 1.0f) {
+    softmax_finite(pr);
+    std::vector<size_t> idx(vocab);
+    for (size_t i = 0; i < vocab; ++i) idx[i] = i;
+    std::stable_sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return pr[a] > pr[b]; });
+    float cum = 0.0f;
+    size_t cutoff = vocab;
+    for (size_t r = 0; r < vocab; ++r) {
+      cum += pr[idx[r]];
+      if (cum >= top_p) {
+        cutoff = r + 1;
+        break;
+      }
+    }
+    std::vector<char> keep(vocab, 0);
+    for (size_t r = 0; r < cutoff; ++r) keep[idx[r]] = 1;
+    for (size_t i = 0; i < vocab; ++i)
+      if (!keep[i]) logits[i] = ninf;
+  }
+  softmax_finite(pr);
+  uint64_t st = seed + (uint64_t)n_past;
+  st = st * 6364136223846793005ULL + 1442695040888963407ULL;
+  const float rf = (float)(st >> 11) / (float)(1ULL << 53);
+  float cum = 0.0f;
+  for (size_t i = 0; i < vocab; ++i) {
+    cum += pr[i];
+    if (rf <= cum) return (uint32_t)i;
+  }
+  return greedy_argmax(pr.data(), vocab);
+}
 
 // ---- model ------------------------------------------------------------------
 void* orc_model_create(const orc_config* c, const orc_weights* w) {

@@ -128,6 +128,38 @@ def kats():
         packed=[0x55, 0x55, 0x55, 0x55, 0x55, 0x55, 0x55, 0b00_11_01_01], packed_rows=2, cols=4, scale=1.0,
         error="QuantizationError", message="(1, 3), shift 4")
 
+    # ---- sample_next_token (crates/bitnet-inference/src/lib.rs:236-390) ----
+    def cfg(temperature=1.0, top_p=1.0, top_k=0, repetition_penalty=1.0, seed=0):
+        return dict(temperature=temperature, top_p=top_p, top_k=top_k, repetition_penalty=repetition_penalty,
+                    seed=seed)
+
+    greedy = cfg(top_k=1, seed=42)  # SamplingConfig::greedy (lib.rs:115-124)
+    add("sample_greedy_argmax", "crates/bitnet-inference/src/lib.rs:1094-1101", fn="sample",
+        logits=[0.1, 0.5, 5.0, 0.2, -1.0], cfg=greedy, past=[], token=2)
+    add("sample_greedy_last_max", "crates/bitnet-inference/src/lib.rs:1104-1110", fn="sample",
+        logits=[0.0, 0.0, 0.0, 0.0, 10.0], cfg=greedy, past=[], token=4)
+    add("sample_greedy_first_max", "crates/bitnet-inference/src/lib.rs:1113-1119", fn="sample",
+        logits=[100.0, 0.0, -1.0, -5.0], cfg=greedy, past=[], token=0)
+    add("sample_only_finite_token", "crates/bitnet-inference/src/lib.rs:1226-1243", fn="sample",
+        logits=["-inf"] * 5 + [1.0] + ["-inf"] * 2, cfg=cfg(), past=[], token=5)
+    add("sample_top_k_1", "crates/bitnet-inference/src/lib.rs:1246-1263", fn="sample",
+        logits=[1.0, 5.0, 0.0, -1.0, 2.0], cfg=cfg(top_k=1), past=[], token=1)
+    add("sample_low_temperature", "crates/bitnet-inference/src/lib.rs:1266-1283", fn="sample",
+        logits=[0.0, 1.0, 10.0, 2.0], cfg=cfg(temperature=0.01), past=[], token=2)
+    add("sample_top_k_3_over_seeds", "crates/bitnet-inference/src/lib.rs:1958-1983", fn="sample",
+        logits=[1.0, 5.0, 3.0, 2.0, 4.0, 0.5], cfg=cfg(temperature=2.0, top_k=3), past=[], seeds=50,
+        allowed=[1, 4, 2])
+    add("sample_in_range", "crates/bitnet-inference/src/lib.rs:1122-1140", fn="sample",
+        logits=[float(f32(i) * f32(0.1)) for i in range(32)], cfg=cfg(temperature=0.8, top_p=0.9, top_k=10, seed=42),
+        past=[], allowed=list(range(32)))
+    add("sample_repetition_penalty", "crates/bitnet-inference/src/lib.rs:1143-1169", fn="sample",
+        logits=[0.0, 0.0, 10.0, 0.0], cfg=cfg(repetition_penalty=1000.0, seed=42), past=[2], allowed=[0, 1, 2, 3])
+    # SamplingConfig::validate (lib.rs:160-178) on the presets and the rejected variants (lib.rs:1024-1090)
+    add("sampling_config_presets", "crates/bitnet-inference/src/lib.rs:1024-1090", fn="sampling_config",
+        valid=["greedy", "chat_defaults", "creative", "default"],
+        invalid=[{"temperature": 0.0}, {"top_p": 1.5}, {"top_p": 0.0}, {"repetition_penalty": 0.9},
+                 {"max_new_tokens": 0}])
+
     # ---- absmax_quantize_row (crates/bitnet-core/src/quant/absmax.rs) ----
     add("absmax_max_is_127", "crates/bitnet-core/src/quant/absmax.rs:291-300", fn="absmax", x=[0.0, 1.0, 2.0, -1.0],
         q_at={"2": 127, "3": -64}, scale=2.0 / 127.0, scale_tol=1e-7)

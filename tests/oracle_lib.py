@@ -42,6 +42,7 @@ _SIGS = {
     "orc_unpack_ternary": (i32, [vp, sz, sz, vp]),
     "orc_absmean_quantize": (i32, [vp, sz, vp, C.POINTER(f32)]),
     "orc_decode_hf_packed": (i32, [vp, sz, sz, sz, f32, vp]),
+    "orc_sample_next_token": (C.c_uint32, [vp, sz, f32, f32, sz, f32, C.c_uint64, vp, sz]),
     "orc_absmax_quantize_row_into": (i32, [vp, sz, vp, sz, C.POINTER(f32)]),
     "orc_quantize_bf16_rows_to_i8": (None, [vp, sz, sz, vp, vp]),
     "orc_bf16_round": (f32, [f32]),
