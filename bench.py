@@ -51,6 +51,9 @@ def args():
     ap.add_argument("--no-prefill", action="store_true", help="skip the C3 ragged-prefill measurement")
     # smaller contexts keep profiler captures of the same kernels to a few GB
     ap.add_argument("--ctx-hi", type=int, default=CTX_HI, help="largest seeded context (default C4's 4096)")
+    ap.add_argument("--workload", choices=["c4", "c5"], default="c4",
+                    help="c4: data-parallel batch-256 decode of the 2B shape (default); c5: the scaled model "
+                         "tensor-parallel over the job's ranks, batch 64 at context 2048")
     return ap.parse_args()
 
 
@@ -536,10 +539,140 @@ def run_cuda(a):
     return 0
 
 
+C5_BATCH, C5_CTX = 64, 2048
+
+
+def run_c5(a):
+    """C5: the scaled model (scaled_model_config: H 4096, 32 layers, 32/8
+    heads, F 14336) tensor-parallel over the N ranks of the job (one GPU
+    each; N = 1 is the plain single-GPU model). 64 sequences at context 2048,
+    bf16 KV; a step is one decode step of all 64. Total work is fixed as N
+    grows ("scaling": "strong"). Every rank holds the full host weights and
+    keeps its share on the device."""
+    import datetime
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, kernel_launches, scaled_model_config, synth, tp
+
+    B, K, W = C5_BATCH, a.steps, a.warmup
+    cfg = scaled_model_config()
+    cfg.max_position_embeddings = C5_CTX + 512
+    t_setup = time.perf_counter()
+    weights = synth.random_model(cfg, seed=SEED)
+    t = tp.init() if dist else None
+    model = BitNetModel(weights, CudaBackend(local), max_batch_tokens=B, tp=t)
+    del weights
+    total_steps = W + K + E2E_STEPS + 2
+    pages = B * ((C5_CTX + total_steps + 15) // 16) + 16
+    kv = model.new_kv_cache(num_pages=pages, max_seqs=B, kv_dtype=KV_BF16)
+    for i in range(B):
+        kv.fill_random(i, C5_CTX, SEED + 17)
+        kv.reserve(i, C5_CTX + total_steps)
+    seqs = np.arange(B, dtype=np.uint32)
+    tok0 = synth.uniform_u32(SEED, 3, B, 0, cfg.vocab_size - 1)
+    d_tok = torch.tensor(tok0.astype(np.int64), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t_setup
+
+    def step():
+        model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            step()
+    torch.cuda.synchronize()
+    model.check()
+    clocks = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.25)
+    launches0 = kernel_launches()
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(K):
+            step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = kernel_launches() - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        tm = torch.tensor([ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    model.check()
+
+    host_tok = d_tok.cpu().numpy().astype(np.uint32)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(E2E_STEPS):
+        host_tok, _ = model.decode_step(kv, seqs, host_tok)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_s = float(te.item())
+
+    # per-rank HBM bytes of one step: the rank's ternary share, the replicated
+    # i8 lm_head, and its KV heads over every cached position
+    H, L, qd, kvd, F, V = (cfg.hidden_size, cfg.num_hidden_layers, cfg.q_dim(), cfg.kv_dim(),
+                           cfg.intermediate_size, cfg.vocab_size)
+    tern = L * ((qd + 2 * kvd) * H + H * qd + 2 * F * H + H * F) / 4
+    kv_bytes = B * (C5_CTX + 1) * L * 2 * kvd * 2
+    rank_bytes = tern / world + V * H + kv_bytes / world
+    peak, peak_kind = peaks()
+    achieved = rank_bytes / (ms / K / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s, scaled model (H 4096, 32 layers, 32/8 heads, F 14336), tensor parallel",
+            "value": B * K / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "i2xi8->i32 matmul, f32 norm/attention, bf16 KV", "data": "synthetic: random-init scaled "
+            "model N(0,0.02) absmean-ternarised; contexts 2048 seeded with N(0,1) bf16 K/V",
+            "config": {"workload": "C5 tensor-parallel decode, scaled model", "global_batch": B, "ctx": C5_CTX,
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "collectives_per_layer": "2 all-gathers (f32 attention / gated FFN rows) + 2 int32 "
+                                                "all-reduces (o, down accumulators), NCCL",
+                       "l2": f"inputs larger than L2 ({kv_bytes / world / 1e9:.1f} GB of KV per rank per step)"},
+            "e2e": {"value": B * E2E_STEPS / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(B * 4 + B * 8),
+                    "d2h_bytes_per_step": int(B * 4), "api": "bitnet_cuda_decode_step", "steps": E2E_STEPS},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step per rank", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_step_per_rank": rank_bytes},
+            "clocks": clk, "gpu_launches": int(launches), "setup_s": round(setup_s, 1),
+        }
+        print(json.dumps(line), flush=True)
+    kv.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = args()
     if a.impl == "reference":
         return run_reference(a)
+    if a.workload == "c5":
+        return run_c5(a)
     return run_cuda(a)
 
 
