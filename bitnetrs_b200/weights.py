@@ -296,3 +296,37 @@ def load_model_config(path: Union[str, Path]) -> ModelConfig:
                        int(j["num_attention_heads"]), int(j.get("num_key_value_heads", j["num_attention_heads"])),
                        int(j["intermediate_size"]), int(j["max_position_embeddings"]),
                        float(j.get("rope_theta", 10000.0)), float(j.get("rms_norm_eps", 1e-5)))
+
+
+def detect_weight_format(path: Union[str, Path]) -> str:
+    """detect_weight_format (crates/bitnet-inference/src/lib.rs:428-452, fn at :438):
+    "packed" when any tensor of the file is U8, else "bf16" (also when the
+    header cannot be read)."""
+    try:
+        p = Path(path)
+        with open(p, "rb") as f:
+            (n,) = struct.unpack("<Q", f.read(8))
+            header = json.loads(f.read(n))
+    except Exception:
+        return "bf16"
+    return "packed" if any(isinstance(m, dict) and m.get("dtype") == "U8" for k, m in header.items()
+                           if k != "__metadata__") else "bf16"
+
+
+def resolve_model_config(model_path: Union[str, Path]) -> ModelConfig:
+    """resolve_model_config (crates/bitnet-inference/src/lib.rs:455-488): the
+    sibling config.json of the checkpoint when it exists, else the 2B config."""
+    from .model import bitnet_2b_config
+
+    cfg = Path(model_path).parent / "config.json"
+    return load_model_config(cfg) if cfg.exists() else bitnet_2b_config()
+
+
+def load_weights(model_path: Union[str, Path], cfg: ModelConfig = None) -> ModelWeights:
+    """What InferenceEngine::new does with a checkpoint (crates/bitnet-inference/src/lib.rs:529-580): the
+    config from resolve_model_config unless given, then the packed or bf16
+    loader by detect_weight_format."""
+    cfg = cfg if cfg is not None else resolve_model_config(model_path)
+    if detect_weight_format(model_path) == "packed":
+        return load_weights_from_packed(model_path, cfg)
+    return load_weights_from_bf16(model_path, cfg)

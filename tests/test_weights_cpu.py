@@ -238,3 +238,29 @@ def test_load_model_config(tmp_path):
                  ' "intermediate_size": 16, "max_position_embeddings": 32}')
     c = Wt.load_model_config(p)
     assert c.num_key_value_heads == 2 and c.rope_theta == 10000.0 and c.rms_norm_eps == 1e-5
+
+
+def test_detect_format_resolve_config_and_load(tmp_path):
+    # detect_weight_format (inference/src/lib.rs:428-452), resolve_model_config
+    # (lib.rs:455-488, tests lib.rs:1359-1400)
+    from bitnetrs_b200 import bitnet_2b_config
+
+    w = synth.random_model(CFG, seed=13)
+    d = tmp_path / "m"
+    d.mkdir()
+    path = d / "model.safetensors"
+    Wt.write_safetensors(path, _packed_checkpoint(w, CFG))
+    assert Wt.detect_weight_format(path) == "packed"
+    assert Wt.resolve_model_config(path) == bitnet_2b_config()  # no sibling config.json
+    (d / "config.json").write_text(
+        '{"vocab_size": 96, "hidden_size": 64, "num_hidden_layers": 2, "num_attention_heads": 4,'
+        ' "num_key_value_heads": 2, "intermediate_size": 128, "max_position_embeddings": 64}')
+    assert Wt.resolve_model_config(path) == CFG
+    got = Wt.load_weights(path)
+    np.testing.assert_array_equal(got.layers[1].down_proj, w.layers[1].down_proj)
+    dense = d / "dense.safetensors"
+    Wt.write_safetensors(dense, {"x": ("F32", (2,), np.zeros(2, np.float32))})
+    assert Wt.detect_weight_format(dense) == "bf16"
+    junk = d / "junk.safetensors"
+    junk.write_bytes(b"\x00\x01")
+    assert Wt.detect_weight_format(junk) == "bf16"
