@@ -299,7 +299,7 @@ def load_model_config(path: Union[str, Path]) -> ModelConfig:
 
 
 def detect_weight_format(path: Union[str, Path]) -> str:
-    """detect_weight_format (crates/bitnet-inference/src/lib.rs:428-452, fn at :438):
+    """detect_weight_format (crates/bitnet-inference/src/lib.rs:428-452):
     "packed" when any tensor of the file is U8, else "bf16" (also when the
     header cannot be read)."""
     try:
@@ -323,9 +323,10 @@ def resolve_model_config(model_path: Union[str, Path]) -> ModelConfig:
 
 
 def load_weights(model_path: Union[str, Path], cfg: ModelConfig = None) -> ModelWeights:
-    """What InferenceEngine::new does with a checkpoint (crates/bitnet-inference/src/lib.rs:529-580): the
-    config from resolve_model_config unless given, then the packed or bf16
-    loader by detect_weight_format."""
+    """What InferenceEngine::new does with a checkpoint
+    (crates/bitnet-inference/src/lib.rs:529-580): the config from
+    resolve_model_config unless given, then the packed or bf16 loader by
+    detect_weight_format."""
     cfg = cfg if cfg is not None else resolve_model_config(model_path)
     if detect_weight_format(model_path) == "packed":
         return load_weights_from_packed(model_path, cfg)
