@@ -262,7 +262,10 @@ void bitnet_cuda_model_destroy(bitnet_cuda_model* model);
  * rank then calls bitnet_cuda_model_create_tp with those bytes and the FULL
  * host weights (collective: all ranks call it together), and every later
  * forward, prefill and decode step on all ranks together with the same
- * batch.  Tensor-parallel steps launch without CUDA-graph capture.
+ * batch.  Tensor-parallel steps launch without CUDA-graph capture.  A
+ * rank's KV cache holds only its KV heads: bitnet_cuda_kv_seq_write / _read
+ * take [layer][pos][local_kv_heads*head_dim] with local_kv_heads =
+ * num_key_value_heads/world.
  * Requirements: num_attention_heads and num_key_value_heads divisible by
  * world, and
  * (hidden_size/num_attention_heads)*num_attention_heads/world and
