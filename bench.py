@@ -51,6 +51,8 @@ def args():
     ap.add_argument("--no-prefill", action="store_true", help="skip the C3 ragged-prefill measurement")
     # smaller contexts keep profiler captures of the same kernels to a few GB
     ap.add_argument("--ctx-hi", type=int, default=CTX_HI, help="largest seeded context (default C4's 4096)")
+    ap.add_argument("--c2", action="store_true",
+                    help="add the C2 op sweep (ternary matmul at M in 1..4096 for each 2B projection shape)")
     ap.add_argument("--workload", choices=["c4", "c5"], default="c4",
                     help="c4: data-parallel batch-256 decode of the 2B shape (default); c5: the scaled model "
                          "tensor-parallel over the job's ranks, batch 64 at context 2048")
@@ -289,6 +291,90 @@ def run_reference(a):
     return 0
 
 
+# C2 op sweep shapes (N x K of each 2B projection) and activation row counts
+C2_SHAPES = [("q/o", 2560, 2560), ("k/v", 640, 2560), ("gate/up", 6912, 2560), ("down", 2560, 6912)]
+C2_M = [1, 8, 64, 512, 4096]
+
+
+def c2_sweep(backend, dev, peak_gbs, min_bytes=320e6):
+    """C2 op sweep: bitnet_cuda_ternary_matmul_device for each 2B projection
+    shape at M quantised activation rows, launched back to back in a CUDA
+    graph that cycles through enough weight copies (> 2x L2) that the weights
+    stream from HBM. Per launch: bytes N*K/4 + M*K + 4M + 4*M*N, ops 2*M*N*K;
+    the bound t* = max(bytes / HBM peak, ops / int8 peak) and frac = t* / t.
+    The int8 tensor peak is twice the measured dense bf16 figure (B200's dense
+    int8 rate is twice its bf16 rate)."""
+    import ctypes as C
+
+    import torch
+
+    from bitnetrs_b200 import _native as N
+    from bitnetrs_b200 import synth
+
+    lib = N.cuda_lib()
+    pk = ROOT / "MEASURED_PEAKS.json"
+    bf16 = float(json.loads(pk.read_text()).get("bf16_tflops", 1590.0)) if pk.exists() else 1590.0
+    tops_peak = 2.0 * bf16
+    out = {"int8_peak_tops": tops_peak, "hbm_peak_gbs": peak_gbs}
+    for name, n, k in C2_SHAPES:
+        packed = synth.ternary_codes(SEED, 19, n, k)
+        wbytes = n * k / 4
+        copies = max(2, int(np.ceil(min_bytes / wbytes)))
+        handles = []
+        for _ in range(copies):
+            h = C.c_void_p()
+            N.check(lib.bitnet_cuda_weight_upload(backend.handle, packed.ctypes.data, packed.size, n, k, 0.0160,
+                                                  C.byref(h)))
+            handles.append(h)
+        ldq = (k + 63) // 64 * 64
+        rows = {}
+        for M in C2_M:
+            xb = synth.bf16_normal(SEED, 20 + M, M * k, 1.0)
+            d_x = torch.from_numpy(xb.view(np.int16).copy()).to(dev)
+            d_xq = torch.zeros(M * ldq, dtype=torch.int8, device=dev)
+            d_amax = torch.zeros(M, dtype=torch.float32, device=dev)
+            d_rs = torch.zeros(M, dtype=torch.int32, device=dev)
+            d_st = torch.zeros(1, dtype=torch.int32, device=dev)
+            d_out = torch.zeros(M * n, dtype=torch.float32, device=dev)
+            s = torch.cuda.Stream(device=dev)
+            torch.cuda.synchronize()
+            N.check(lib.bitnet_cuda_quantize_rows_device(backend.handle, d_x.data_ptr(), 1, M, k, d_xq.data_ptr(),
+                                                         ldq, d_amax.data_ptr(), d_rs.data_ptr(), d_st.data_ptr(),
+                                                         C.c_void_p(s.cuda_stream)))
+            torch.cuda.synchronize()
+            reps = 2 * copies
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(reps):
+                    N.check(lib.bitnet_cuda_ternary_matmul_device(backend.handle, handles[i % copies],
+                                                                  d_xq.data_ptr(), ldq, d_amax.data_ptr(),
+                                                                  d_rs.data_ptr(), M, d_out.data_ptr(), None,
+                                                                  C.c_void_p(s.cuda_stream)))
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                e0.record(s)
+                for _ in range(3):
+                    g.replay()
+                e1.record(s)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / (3 * reps)
+            b = wbytes + M * k + 4 * M + 4 * M * n
+            ops = 2.0 * M * n * k
+            t_star = max(b / (peak_gbs * 1e9), ops / (tops_peak * 1e12))
+            rows[str(M)] = {"us_per_launch": round(ms * 1e3, 3), "gbs": round(b / (ms / 1e3) / 1e9, 1),
+                            "tops": round(ops / (ms / 1e3) / 1e12, 2),
+                            "bound": "hbm" if b / (peak_gbs * 1e9) >= ops / (tops_peak * 1e12) else "int8 tensor",
+                            "frac": round(t_star / (ms / 1e3), 3)}
+            del g
+        out[name] = {"N": n, "K": k, "M": rows}
+        for h in handles:
+            lib.bitnet_cuda_weight_destroy(h)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
@@ -485,6 +571,9 @@ def run_cuda(a):
     if rank == 0 and not a.no_gemv_sweep:
         gemv_m1 = gemv_sweep(backend, dev, peak)
 
+    # ---- C2 op sweep (rank 0, on request) ----
+    c2 = c2_sweep(backend, dev, peak) if rank == 0 and a.c2 else None
+
     # ---- C3 ragged prefill (rank 0, N=1) ----
     prefill = None
     if rank == 0 and world == 1 and not a.no_prefill:
@@ -519,6 +608,7 @@ def run_cuda(a):
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": attn_bytes,
                          "avg_launch_ms": attn_launch_ms},
             "gemv_m1": gemv_m1,
+            "c2": c2,
             "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32; tcgen05 kind::i8 for the batch-256 step, dp4a GEMV at batch 1)", "ms_per_step": mm_ms,
                      "launches": mm_n, "hbm_gbs": (w_bytes + act_bytes) / (mm_ms / 1e3) / 1e9 if mm_ms else None,
                      "tops": mm_ops / (mm_ms / 1e3) / 1e12 if mm_ms else None},
