@@ -128,3 +128,13 @@ def test_kv_normal_moments():
     assert k.shape == (2, 100, 32)
     assert abs(k.mean()) < 0.05 and abs(k.std() - 1.0) < 0.05
     assert not np.array_equal(k, v)
+
+
+@pytest.mark.parametrize("lang,std", [("c", "-std=c99"), ("c++", "-std=c++17")])
+def test_header_compiles_as_plain_c_and_cpp(lang, std):
+    # the boundary is consumed through FFIs (Rust bindgen/extern "C", ctypes),
+    # so the header must stand alone as C99 as well as C++
+    cc = "gcc" if lang == "c" else "g++"
+    r = subprocess.run([cc, std, "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x", lang, str(HEADER)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
