@@ -5,17 +5,27 @@ Default workload (continuous-batching decode): the 2B
 architecture with random-init weights (N(0,0.02), absmean-ternarised, packed
 in the reference format), 256 concurrent sequences per GPU whose contexts are
 seeded with lengths U[128, 4096] and N(0,1) bf16 K/V, greedy decode.  A step
-is one decode step of all 256 sequences.  Data parallel: every rank owns its
-own 256 sequences and a full weight replica; there is no collective on the
-data path ("scaling": "weak").
+is one decode step of all 256 sequences.  Data parallel: every rank decodes
+256 sequences of one seeded pool, placed by KV positions, with a full weight
+replica; there is no collective on the data path ("scaling": "weak").
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
 `value` is device-timed (CUDA events on the launching stream, max over ranks)
 with weights, KV and tokens resident in HBM; `e2e` is the same metric through
 the host-buffer C-ABI call bitnet_cuda_decode_step (token ids in from host,
-next-token ids out to host every step).  `--impl reference` times the CPU
-restatement of the reference backend (oracle/) on the host cores.
+next-token ids out to host every step).  The same line carries:
+
+* `parity` (N = 1): 8 sampled sequences of the batch-256 step decoded by the
+  CPU oracle on the GPU's tokens, greedy tokens and logits compared; the same
+  decode is the timed `cpu_baseline`;
+* `strong` (N > 1): the N = 1 workload's 256 sequences split over the ranks;
+* `c5` (N > 1): the scaled model tensor-parallel over the ranks;
+* `c2` (N = 1): the ternary matmul op sweep, M in {1, 8, 64, 512, 4096};
+* `gemv_m1`, `batch1`, `prefill` (C3), per-kernel-class times.
+
+`--impl reference` times the CPU restatement of the reference backend
+(oracle/) on the host cores.
 """
 from __future__ import annotations
 
@@ -51,8 +61,10 @@ def args():
     ap.add_argument("--no-prefill", action="store_true", help="skip the C3 ragged-prefill measurement")
     # smaller contexts keep profiler captures of the same kernels to a few GB
     ap.add_argument("--ctx-hi", type=int, default=CTX_HI, help="largest seeded context (default C4's 4096)")
-    ap.add_argument("--c2", action="store_true",
-                    help="add the C2 op sweep (ternary matmul at M in 1..4096 for each 2B projection shape)")
+    ap.add_argument("--no-c2", action="store_true",
+                    help="skip the C2 op sweep (ternary matmul at M in 1..4096 for each 2B projection shape)")
+    ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling C4 measurement (N > 1)")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 tensor-parallel measurement (N > 1)")
     ap.add_argument("--workload", choices=["c4", "c5"], default="c4",
                     help="c4: data-parallel batch-256 decode of the 2B shape (default); c5: the scaled model "
                          "tensor-parallel over the job's ranks, batch 64 at context 2048")
@@ -207,36 +219,52 @@ def gemv_sweep(backend, dev, peak_gbs, min_bytes=320e6):
 # ---------------------------------------------------------------------------
 # CPU side: the oracle (restatement of the reference CPU backend)
 # ---------------------------------------------------------------------------
-def cpu_decode_sample(weights, cfg, ctxs, rank_seed, budget_s=15.0, max_tokens=32, warm=1):
-    """Greedy-decode tokens on seeded contexts with the oracle; returns (tok/s, tokens, seconds, threads)."""
+PARITY_ROWS, PARITY_STEPS = 8, 16  # sampled sequences x teacher-forced decode steps
+
+
+def parity_rows(batch, n=PARITY_ROWS):
+    """Rows of the batch sampled for the oracle check: evenly spaced."""
+    return sorted(set(np.linspace(0, batch - 1, min(n, batch)).astype(int).tolist()))
+
+
+def cpu_parity(weights, ctxs, rows, host_kv, rec_in, rec_out, rec_logits):
+    """The oracle decodes each sampled sequence one after another (the
+    reference's engine is batch-1 and sequence-serial) from the same seeded
+    context, fed the GPU's input token of every step (teacher forcing): its
+    greedy token is compared with the GPU's at every step and its logits with
+    the GPU's rows at the recorded steps. Only the forward calls are timed.
+    Returns (tokens/s, tokens, seconds, threads, parity dict)."""
     sys.path.insert(0, str(ROOT / "tests"))
     import oracle_lib as O
-    from bitnetrs_b200 import synth
 
     om = O.OracleModel(weights)
-    kvs, toks = [], []
-    for i, n in enumerate(ctxs):
-        kv = om.kv(n + max_tokens + warm + 2, bf16=True)
-        k, v = synth.kv_normal(rank_seed, i, cfg, n)
-        kv.seed(k, v)
-        kvs.append((kv, n))
-        toks.append(int(synth.uniform_u32(rank_seed, 3, len(ctxs), 0, cfg.vocab_size - 1)[i]))
-    pos = [n for _, n in kvs]
     L = O.lib()
-    for _ in range(warm):
-        for i, (kv, _) in enumerate(kvs):
-            lg = om.forward(kv, [toks[i]], pos[i])
-            toks[i] = L.orc_greedy_argmax(O.p(lg), lg.size)
-            pos[i] += 1
-    done, t0 = 0, time.perf_counter()
-    while done < max_tokens and (time.perf_counter() - t0) < budget_s:
-        for i, (kv, _) in enumerate(kvs):
-            lg = om.forward(kv, [toks[i]], pos[i])
-            toks[i] = L.orc_greedy_argmax(O.p(lg), lg.size)
-            pos[i] += 1
-            done += 1
-    dt = time.perf_counter() - t0
-    return done / dt, done, dt, int(L.orc_threads())
+    n = eq = 0
+    dt, rel = 0.0, 0.0
+    mism = []
+    for j, i in enumerate(rows):
+        c = int(ctxs[i])
+        okv = om.kv(c + PARITY_STEPS + 2, bf16=True)
+        okv.seed(*host_kv.pop(i))
+        for s in range(len(rec_in)):
+            t0 = time.perf_counter()
+            lg = om.forward(okv, [int(rec_in[s][j])], c + s)
+            dt += time.perf_counter() - t0
+            tok = int(L.orc_greedy_argmax(O.p(lg), lg.size))
+            n += 1
+            if tok == int(rec_out[s][j]):
+                eq += 1
+            elif len(mism) < 8:
+                mism.append({"row": int(i), "step": s, "oracle": tok, "gpu": int(rec_out[s][j])})
+            if s in rec_logits:
+                rel = max(rel, float(np.max(np.abs(rec_logits[s][j] - lg)) / float(np.max(np.abs(lg)))))
+        del okv
+    par = {"rows": [int(r) for r in rows], "contexts": [int(ctxs[r]) for r in rows], "steps": len(rec_in),
+           "tokens_checked": n, "tokens_equal": eq, "all_tokens_equal": eq == n,
+           "max_rel_logit": rel, "logit_steps": sorted(int(k) for k in rec_logits), "mismatches": mism,
+           "method": "oracle fed the GPU's input tokens (teacher forcing) from the same seeded bf16 contexts; "
+                     "greedy tokens compared every step, logits (max|d| / max|ref|) at the recorded steps"}
+    return n / dt, n, dt, int(L.orc_threads()), par
 
 
 def run_reference(a):
@@ -247,26 +275,30 @@ def run_reference(a):
 
     cfg = model_config()
     weights = synth.random_model(cfg, seed=SEED)
-    ctxs = synth.uniform_u32(SEED, 11, 2, CTX_LO, CTX_HI).tolist()
+    ctx_all = synth.uniform_u32(SEED, 11, a.batch, CTX_LO, CTX_HI)
+    rows = parity_rows(a.batch)
+    ctxs = [int(ctx_all[i]) for i in rows]
     sys.path.insert(0, str(ROOT / "tests"))
     import oracle_lib as O
 
     om = O.OracleModel(weights)
+    tok_all = synth.uniform_u32(SEED, 3, a.batch, 0, cfg.vocab_size - 1)
     kvs, toks, pos = [], [], []
-    for i, n in enumerate(ctxs):
+    for i, n in zip(rows, ctxs):
         kv = om.kv(n + a.steps + a.warmup + 2, bf16=True)
         k, v = synth.kv_normal(SEED, i, cfg, n)
         kv.seed(k, v)
+        del k, v
         kvs.append(kv)
         pos.append(n)
-        toks.append(int(synth.uniform_u32(SEED, 3, 2, 0, cfg.vocab_size - 1)[i]))
+        toks.append(int(tok_all[i]))
     L = O.lib()
 
     def step():
-        for i, kv in enumerate(kvs):
-            lg = om.forward(kv, [toks[i]], pos[i])
-            toks[i] = L.orc_greedy_argmax(O.p(lg), lg.size)
-            pos[i] += 1
+        for j, kv in enumerate(kvs):
+            lg = om.forward(kv, [toks[j]], pos[j])
+            toks[j] = L.orc_greedy_argmax(O.p(lg), lg.size)
+            pos[j] += 1
 
     for _ in range(a.warmup):
         step()
@@ -275,8 +307,8 @@ def run_reference(a):
         step()
     dt = time.perf_counter() - t0
     v = len(kvs) * a.steps / dt
-    sample = (f"{len(kvs)} sequences (contexts {ctxs}) x {a.steps} greedy decode steps, sequence-serial "
-              "like the reference (one engine per sequence)")
+    sample = (f"{len(kvs)} of the 256 seeded C4 sequences (rows {rows}, contexts {ctxs}) x {a.steps} greedy "
+              "decode steps, sequence-serial like the reference (one engine per sequence)")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -420,6 +452,43 @@ def prefill_c3(weights, backend, cfg, seed):
                    "attention, tcgen05 ternary GEMM"}
 
 
+def timed_decode(model, kv, seqs, d_tok, stream, K, W, dist, dev):
+    """W untimed then K timed device-resident decode steps (CUDA graphs),
+    bracketed by a barrier and a synchronise; returns the max over ranks of
+    the timed region in ms and the kernels launched inside it."""
+    import torch
+
+    from bitnetrs_b200 import kernel_launches
+
+    def step():
+        model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            step()
+    torch.cuda.synchronize()
+    model.check()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = kernel_launches()
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(K):
+            step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = kernel_launches() - launches0
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    model.check()
+    return ms, launches
+
+
 def run_cuda(a):
     import torch
 
@@ -436,7 +505,8 @@ def run_cuda(a):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
 
-    from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, kernel_launches, synth
+    from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, synth
+    from bitnetrs_b200.dp import shard_loads, shard_requests, shard_requests_equal
 
     B, K, W = a.batch, a.steps, a.warmup
     cfg = model_config(a.ctx_hi)
@@ -444,56 +514,58 @@ def run_cuda(a):
     weights = synth.random_model(cfg, seed=SEED)
     backend = CudaBackend(local)
     model = BitNetModel(weights, backend, max_batch_tokens=max(B, 256))
+    # Weak scaling: B sequences per GPU. The job's B * world contexts come from
+    # one seeded pool and are placed B per rank, balanced by KV positions
+    # (bitnetrs_b200.dp); at N = 1 this is the seeded C4 batch itself.
     rank_seed = SEED + 1000 * rank
-    ctxs = synth.uniform_u32(rank_seed, 11, B, CTX_LO, a.ctx_hi).astype(np.int64)
-    total_steps = W + K + 3 + E2E_STEPS + 2
+    pool = synth.uniform_u32(SEED, 11, B * world, CTX_LO, a.ctx_hi).astype(np.int64)
+    placement = shard_requests_equal(pool.tolist(), world, B)
+    ctxs = pool[placement[rank]]
+    cpu_leg = rank == 0 and world == 1 and not a.no_cpu_baseline
+    prow = parity_rows(B) if cpu_leg else []
+    total_steps = PARITY_STEPS + W + K + 3 + E2E_STEPS + 2
     pages = int(np.sum((ctxs + total_steps + 15) // 16)) + 64 + (128 + 64 + 15) // 16
     kv = model.new_kv_cache(num_pages=pages, max_seqs=B + 1, kv_dtype=KV_BF16)
+    host_kv = {}
     for i in range(B):
-        kv.fill_random(i, int(ctxs[i]), rank_seed)
+        if i in prow:
+            # the oracle's rows: host-generated values written to the cache,
+            # so both sides hold the same bf16 context
+            k, v = synth.kv_normal(rank_seed, i, cfg, int(ctxs[i]))
+            kv.write(i, k, v)
+            host_kv[i] = (k, v)
+        else:
+            kv.fill_random(i, int(ctxs[i]), rank_seed)
         kv.reserve(i, int(ctxs[i]) + total_steps)
     seqs = np.arange(B, dtype=np.uint32)
     dev = torch.device("cuda", local)
     tok0 = synth.uniform_u32(rank_seed, 3, B, 0, cfg.vocab_size - 1)
-    d_tok = torch.tensor(tok0.astype(np.int64), dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t_setup
     print(f"[bench] setup {setup_s:.1f}s, pages {pages}, mean ctx {ctxs.mean():.0f}", file=sys.stderr, flush=True)
 
-    def step():
-        model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
-
-    with torch.cuda.stream(stream):
-        for _ in range(W):
-            step()
-    torch.cuda.synchronize()
-    model.check()
+    # ---- parity steps: the batch-B step through the host API, sampled rows recorded ----
+    host_tok = tok0.astype(np.uint32)
+    rec_in, rec_out, rec_logits = [], [], {}
+    for s in range(PARITY_STEPS):
+        want = bool(prow) and s in (0, PARITY_STEPS - 1)
+        nxt, lg = model.decode_step(kv, seqs, host_tok, want_logits=want)
+        if prow:
+            rec_in.append(host_tok[prow].copy())
+            rec_out.append(nxt[prow].copy())
+            if want:
+                rec_logits[s] = lg[prow].copy()
+        host_tok = nxt
+        del lg
+    d_tok = torch.tensor(host_tok.astype(np.int64), dtype=torch.int32, device=dev)
 
     # ---- timed region: K device-resident decode steps ----
     clocks = Clocks(local)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.25)  # at least one sample before load
-    launches0 = kernel_launches()
-    ev0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(K):
-            step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    launches = kernel_launches() - launches0
+    ms, launches = timed_decode(model, kv, seqs, d_tok, stream, K, W, dist, dev)
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    model.check()
     ms_per_step = ms / K
     value = world * B * K / (ms / 1e3)
 
@@ -501,8 +573,8 @@ def run_cuda(a):
     model.set_kernel_timing(True)
     ctx_before = np.array([kv.len(i) for i in range(B)], dtype=np.int64)
     with torch.cuda.stream(stream):
-        step()  # capture + run
-        step()
+        for _ in range(2):  # capture + run, run
+            model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
     torch.cuda.synchronize()
     kt = model.kernel_times()
     model.set_kernel_timing(False)
@@ -512,7 +584,7 @@ def run_cuda(a):
     attn_bytes = float(np.sum(ctx_at) * nkv * hd * 2 * 2 + 2 * B * H * 4)
     attn_kernel = model.attention_kernel(kv, B)
     attn_ms, attn_n = kt["attention"]
-    attn_launch_ms = attn_ms / max(attn_n, 1) * 1.0
+    attn_launch_ms = attn_ms / max(attn_n, 1)
     attn_gbs = attn_bytes / (attn_launch_ms / 1e3) / 1e9 if attn_n else None
     peak, peak_kind = peaks()
     # ternary matmul: weight stream per step + int8 activations + f32 outputs
@@ -540,7 +612,6 @@ def run_cuda(a):
            "api": "bitnet_cuda_decode_step (host token ids in, greedy next ids out)", "steps": E2E_STEPS}
 
     # ---- batch-1 decode, same model ----
-    b1 = None
     s1 = B  # spare sequence slot
     kv.fill_random(s1, 128, rank_seed + 7)
     kv.reserve(s1, 128 + 40)
@@ -562,31 +633,67 @@ def run_cuda(a):
     torch.cuda.synchronize()
     kt1 = model.kernel_times()
     model.set_kernel_timing(False)
+    per_tok = 521011200 + 328335360 + 513024 + 76800 * 160 + 5120  # SURVEY 8(d) C1 bytes per token at context 160
     b1 = {"value": 1e3 / b1_ms, "unit": "tokens/s", "ms_per_token": b1_ms, "context": "128..160",
-          "kernels_ms_per_token": {k: round(v[0], 4) for k, v in kt1.items()}}
+          "hbm_gbs": per_tok / (b1_ms / 1e3) / 1e9, "frac": per_tok / (b1_ms / 1e3) / 1e9 / peak,
+          "kernels_ms_per_token": {k: round(v[0], 4) for k, v in kt1.items()},
+          "note": "kernels_ms_per_token comes from events around every launch, which break the overlap of "
+                  "dependent launches; their sum exceeds ms_per_token"}
     model.check()
+    kv.close()
+
+    # ---- strong scaling (N > 1): the N = 1 workload's 256 sequences over the job's ranks ----
+    strong = {"value": value, "unit": "tokens/s", "global_batch": B, "ms_per_step": ms_per_step,
+              "note": "N = 1: the same sequences as value"} if world == 1 else None
+    if world > 1 and not a.no_strong:
+        pool1 = synth.uniform_u32(SEED, 11, B, CTX_LO, a.ctx_hi).astype(np.int64)
+        shards = shard_requests(pool1.tolist(), world)
+        mine = shards[rank]
+        steps2 = W + K + 2
+        kv2 = model.new_kv_cache(num_pages=int(np.sum((pool1[mine] + steps2 + 15) // 16)) + 16,
+                                 max_seqs=max(1, len(mine)), kv_dtype=KV_BF16)
+        for j, i in enumerate(mine):
+            kv2.fill_random(j, int(pool1[i]), SEED + 17)
+            kv2.reserve(j, int(pool1[i]) + steps2)
+        seqs2 = np.arange(len(mine), dtype=np.uint32)
+        d_tok2 = torch.tensor(synth.uniform_u32(SEED, 3, B, 0, cfg.vocab_size - 1)[mine].astype(np.int64),
+                              dtype=torch.int32, device=dev)
+        ms2, _ = timed_decode(model, kv2, seqs2, d_tok2, stream, K, W, dist, dev)
+        kv2.close()
+        strong = {"value": B * K / (ms2 / 1e3), "unit": "tokens/s", "global_batch": B, "ms_per_step": ms2 / K,
+                  "rows_per_rank": [len(x) for x in shards], "kv_positions_per_rank": shard_loads(pool1.tolist(),
+                                                                                                  shards),
+                  "placement": "bitnetrs_b200.dp.shard_requests (longest context first to the least-loaded rank)"}
 
     # ---- decode GEMV sweep (rank 0) ----
     gemv_m1 = None
     if rank == 0 and not a.no_gemv_sweep:
         gemv_m1 = gemv_sweep(backend, dev, peak)
 
-    # ---- C2 op sweep (rank 0, on request) ----
-    c2 = c2_sweep(backend, dev, peak) if rank == 0 and a.c2 else None
+    # ---- C2 op sweep (rank 0, N = 1) ----
+    c2 = c2_sweep(backend, dev, peak) if rank == 0 and world == 1 and not a.no_c2 else None
 
-    # ---- C3 ragged prefill (rank 0, N=1) ----
+    # ---- C3 ragged prefill (rank 0, N = 1) ----
     prefill = None
     if rank == 0 and world == 1 and not a.no_prefill:
         prefill = prefill_c3(weights, backend, cfg, rank_seed)
+    model.close()
 
-    # ---- CPU baseline (rank 0, N=1) ----
-    cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        ctx_sample = [int(c) for c in ctxs[:2]]
-        v, n, dt, thr = cpu_decode_sample(weights, cfg, ctx_sample, rank_seed)
+    # ---- C5 tensor parallelism over the job's ranks (N > 1) ----
+    c5 = None
+    if world > 1 and not a.no_c5:
+        weights = None  # the 2B host weights are not needed past this point at N > 1
+        c5 = c5_measure(a, dist, world, rank, local, dev)
+
+    # ---- CPU baseline and parity of the sampled rows (rank 0, N = 1) ----
+    cpu, parity = None, None
+    if cpu_leg:
+        v, n, dt, thr, parity = cpu_parity(weights, ctxs, prow, host_kv, rec_in, rec_out, rec_logits)
         cpu = {"value": v, "unit": "tokens/s", "cores": thr, "kind": "port",
-               "sample": f"{n} greedy decode tokens over 2 of the seeded sequences (contexts {ctx_sample}), "
-                         f"sequence-serial like the reference, {dt:.1f} s"}
+               "sample": f"{n} decode tokens: {len(prow)} of the {B} seeded sequences (rows {prow}, contexts "
+                         f"{[int(ctxs[i]) for i in prow]}) x {PARITY_STEPS} steps fed the GPU's tokens, "
+                         f"sequence-serial like the reference, {dt:.1f} s of forward calls; the same tokens are "
+                         "the parity sample"}
 
     if rank == 0:
         line = {
@@ -596,9 +703,11 @@ def run_cuda(a):
             "data": "synthetic: random-init 2B weights N(0,0.02) absmean-ternarised; contexts U[128,4096] "
                     "seeded with N(0,1) bf16 K/V",
             "config": {"workload": "C4 continuous-batching decode, BitNet-2B shape", "batch_per_gpu": B,
-                       "global_batch": B * world, "ctx": f"U[{CTX_LO},{a.ctx_hi}] seeded per rank",
-                       "kv": "paged bf16, 16-token pages", "parallelism": f"dp{world} (replicated weights, no "
-                                                                         f"collective)",
+                       "global_batch": B * world, "ctx": f"U[{CTX_LO},{a.ctx_hi}] seeded",
+                       "kv": "paged bf16, 16-token pages",
+                       "parallelism": f"dp{world} (replicated weights, no collective)",
+                       "placement": "B * N seeded contexts, B per rank balanced by KV positions "
+                                    "(bitnetrs_b200.dp.shard_requests_equal)",
                        "l2": f"inputs larger than L2 ({attn_bytes * L / 1e9:.1f} GB of KV read per step)"},
             "e2e": e2e,
             "roofline": {"bound": "hbm", "kernel": attn_kernel,
@@ -607,9 +716,13 @@ def run_cuda(a):
                          "traffic": traffic_from_profiles(attn_kernel),
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": attn_bytes,
                          "avg_launch_ms": attn_launch_ms},
+            "parity": parity,
+            "strong": strong,
             "gemv_m1": gemv_m1,
             "c2": c2,
-            "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32; tcgen05 kind::i8 for the batch-256 step, dp4a GEMV at batch 1)", "ms_per_step": mm_ms,
+            "c5": c5,
+            "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32; tcgen05 kind::i8 for the batch-256 step, dp4a GEMV "
+                               "at batch 1)", "ms_per_step": mm_ms,
                      "launches": mm_n, "hbm_gbs": (w_bytes + act_bytes) / (mm_ms / 1e3) / 1e9 if mm_ms else None,
                      "tops": mm_ops / (mm_ms / 1e3) / 1e12 if mm_ms else None},
             "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kt.items()},
@@ -621,8 +734,6 @@ def run_cuda(a):
             "setup_s": round(setup_s, 1),
         }
         print(json.dumps(line), flush=True)
-    kv.close()
-    model.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -632,34 +743,22 @@ def run_cuda(a):
 C5_BATCH, C5_CTX = 64, 2048
 
 
-def run_c5(a):
+def c5_measure(a, dist, world, rank, local, dev):
     """C5: the scaled model (scaled_model_config: H 4096, 32 layers, 32/8
     heads, F 14336) tensor-parallel over the N ranks of the job (one GPU
     each; N = 1 is the plain single-GPU model). 64 sequences at context 2048,
     bf16 KV; a step is one decode step of all 64. Total work is fixed as N
     grows ("scaling": "strong"). Every rank holds the full host weights and
-    keeps its share on the device."""
-    import datetime
-
+    keeps its share on the device. Returns rank 0's result (None elsewhere)."""
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
-    from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, kernel_launches, scaled_model_config, synth, tp
+    from bitnetrs_b200 import KV_BF16, BitNetModel, CudaBackend, scaled_model_config, synth, tp
 
     B, K, W = C5_BATCH, a.steps, a.warmup
     cfg = scaled_model_config()
     cfg.max_position_embeddings = C5_CTX + 512
     t_setup = time.perf_counter()
-    weights = synth.random_model(cfg, seed=SEED)
+    weights = synth.random_model_iid(cfg, seed=SEED)
     t = tp.init() if dist else None
     model = BitNetModel(weights, CudaBackend(local), max_batch_tokens=B, tp=t)
     del weights
@@ -675,37 +774,11 @@ def run_c5(a):
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t_setup
-
-    def step():
-        model.decode_step_device(kv, seqs, d_tok.data_ptr(), d_tok.data_ptr(), 0, stream.cuda_stream)
-
-    with torch.cuda.stream(stream):
-        for _ in range(W):
-            step()
-    torch.cuda.synchronize()
-    model.check()
     clocks = Clocks(local)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.25)
-    launches0 = kernel_launches()
-    ev0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(K):
-            step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    launches = kernel_launches() - launches0
+    ms, launches = timed_decode(model, kv, seqs, d_tok, stream, K, W, dist, dev)
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        tm = torch.tensor([ms], device=dev)
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        ms = float(tm.item())
-    model.check()
 
     host_tok = d_tok.cpu().numpy().astype(np.uint32)
     if dist:
@@ -719,6 +792,8 @@ def run_c5(a):
         te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_s = float(te.item())
+    kv.close()
+    model.close()
 
     # per-rank HBM bytes of one step: the rank's ternary share, the replicated
     # i8 lm_head, and its KV heads over every cached position
@@ -729,28 +804,48 @@ def run_c5(a):
     rank_bytes = tern / world + V * H + kv_bytes / world
     peak, peak_kind = peaks()
     achieved = rank_bytes / (ms / K / 1e3) / 1e9
+    if rank != 0:
+        return None
+    return {
+        "metric": "decode tokens/s, scaled model (H 4096, 32 layers, 32/8 heads, F 14336), tensor parallel",
+        "value": B * K / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "i2xi8->i32 matmul, f32 norm/attention, bf16 KV",
+        "data": "synthetic: random-init scaled model, ternary codes drawn with the distribution absmean "
+                "ternarisation of N(0,0.02) gives (P(0) 0.310, per-tensor scale 0.02*sqrt(2/pi)); contexts 2048 "
+                "seeded with N(0,1) bf16 K/V",
+        "config": {"workload": "C5 tensor-parallel decode, scaled model", "global_batch": B, "ctx": C5_CTX,
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "collectives_per_layer": "2 all-gathers (f32 attention / gated FFN rows) + 2 int32 "
+                                            "all-reduces (o, down accumulators), NCCL",
+                   "l2": f"inputs larger than L2 ({kv_bytes / world / 1e9:.1f} GB of KV per rank per step)"},
+        "e2e": {"value": B * E2E_STEPS / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(B * 4 + B * 8),
+                "d2h_bytes_per_step": int(B * 4), "api": "bitnet_cuda_decode_step", "steps": E2E_STEPS},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step per rank", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_step_per_rank": rank_bytes},
+        "clocks": clk, "gpu_launches": int(launches), "setup_s": round(setup_s, 1),
+    }
+
+
+def run_c5(a):
+    import datetime
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    line = c5_measure(a, dist, world, rank, local, dev)
     if rank == 0:
-        line = {
-            "metric": "decode tokens/s, scaled model (H 4096, 32 layers, 32/8 heads, F 14336), tensor parallel",
-            "value": B * K / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "i2xi8->i32 matmul, f32 norm/attention, bf16 KV", "data": "synthetic: random-init scaled "
-            "model N(0,0.02) absmean-ternarised; contexts 2048 seeded with N(0,1) bf16 K/V",
-            "config": {"workload": "C5 tensor-parallel decode, scaled model", "global_batch": B, "ctx": C5_CTX,
-                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
-                       "collectives_per_layer": "2 all-gathers (f32 attention / gated FFN rows) + 2 int32 "
-                                                "all-reduces (o, down accumulators), NCCL",
-                       "l2": f"inputs larger than L2 ({kv_bytes / world / 1e9:.1f} GB of KV per rank per step)"},
-            "e2e": {"value": B * E2E_STEPS / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(B * 4 + B * 8),
-                    "d2h_bytes_per_step": int(B * 4), "api": "bitnet_cuda_decode_step", "steps": E2E_STEPS},
-            "roofline": {"bound": "hbm", "kernel": "whole decode step per rank", "achieved": achieved, "peak": peak,
-                         "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_step_per_rank": rank_bytes},
-            "clocks": clk, "gpu_launches": int(launches), "setup_s": round(setup_s, 1),
-        }
         print(json.dumps(line), flush=True)
-    kv.close()
-    model.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -187,6 +187,19 @@ int exact3_make_tmap(const KvGeom& kv, CUtensorMap* map);  // 0 on success
 void launch_paged_attention_exact3(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
                                    const int32_t* page_table, const KvGeom& kv, const CUtensorMap& map, int layer,
                                    int max_ctx, float* out, const ExpTable& et, int32_t* status, cudaStream_t st);
+// The same computation as two streaming kernels per layer (kernels_attn_x4.cu):
+// QK + softmax per (token, kv head), then PV per (token, kv head), through
+// `scratch` (attn_x4_scratch_floats floats).  `order` (T entries, may be
+// null) lists the tokens in the order their CTAs start (longest context
+// first).  Uses the pool's tensor map (exact3_make_tmap).
+bool attn_x4_supported(const KvGeom& kv, int nh);
+size_t attn_x4_scratch_floats(int T, int kv_heads, int max_ctx);
+size_t attn_x4_smem(int max_ctx);
+int attn_x4_prepare(int max_ctx);  // outside graph capture; 0 on success
+void launch_attn_x4(const float* q, int T, int nh, const int32_t* tok_pos, const int32_t* tok_seq,
+                    const int32_t* order, const int32_t* page_table, const KvGeom& kv, const CUtensorMap& map,
+                    int layer, int max_ctx, float* out, float* scratch, const ExpTable& et, int32_t* status,
+                    cudaStream_t st);
 // Candidates for the exp exception table: bit patterns u in [lo, hi] whose
 // double-evaluated exp lands within 0.003 ulp of a float rounding midpoint;
 // writes (u, (float)exp((double)x)) pairs and counts them in *count.

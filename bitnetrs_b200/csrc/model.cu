@@ -44,6 +44,8 @@ struct bitnet_cuda_model {
   size_t exact2_smem_max = 0;
   bool exact3_ok = false;    // same for the TMA-fed variant
   size_t exact3_smem_max = 0;
+  bool x4_ok = false;        // same for the two-kernel (QK + softmax, PV) variant
+  size_t x4_smem_max = 0;
   uint16_t* a3 = nullptr;    // [R][3H] bf16 split of the final-normed rows
   int numerics = BITNET_NUMERICS_AUTO;
   std::vector<Layer> layers;
@@ -59,10 +61,10 @@ struct bitnet_cuda_model {
   float* amax = nullptr;
   int32_t* rowsum = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;
-  int32_t *tok_pos = nullptr, *tok_seq = nullptr, *last_row = nullptr, *status = nullptr;
+  int32_t *tok_pos = nullptr, *tok_seq = nullptr, *last_row = nullptr, *order = nullptr, *status = nullptr;
   DevBuf partial;
   // pinned staging
-  int32_t* h_meta = nullptr;  // [2*Tmax + Tmax] pos, seq, last_row
+  int32_t* h_meta = nullptr;  // [4 * Tmax]: pos, seq, last_row, order (tokens by descending position)
   uint32_t* h_tokens = nullptr;
   // captured decode graphs, keyed by (kv, batch, timed), with their kernel
   // counts and (when timed) the event pairs recorded around each launch
@@ -207,6 +209,9 @@ bool use_mma_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int
 bool use_exact2_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
   return m->exact2_ok && exact2_supported(kv->g, m->nh) && exact2_smem(max_ctx) <= m->exact2_smem_max;
 }
+bool use_x4_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
+  return m->x4_ok && kv->tmap_ok && attn_x4_supported(kv->g, m->nh) && attn_x4_smem(max_ctx) <= m->x4_smem_max;
+}
 bool use_exact3_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
   return m->exact3_ok && kv->tmap_ok && exact3_supported(kv->g, m->nh) && exact3_smem(max_ctx) <= m->exact3_smem_max;
 }
@@ -302,7 +307,10 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
     // a tensor-parallel rank writes its heads straight into its all-gather slot
     float* attn_out = m->tp ? m->tp_gath + (size_t)m->tp_rank * T * qd : m->attn;
     timed(m, kAttn, st, [&] {
-      if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx))
+      if (use_exact_attention(m, T) && use_x4_attention(m, kv, max_ctx))
+        launch_attn_x4(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, m->order, kv->d_table, kv->g, kv->tmap, l, max_ctx,
+                       attn_out, m->partial.as<float>(), m->ctx->exp_table, m->status, st);
+      else if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx))
         launch_paged_attention_exact3(m->qrot, T, m->nh, m->tok_pos, m->tok_seq, kv->d_table, kv->g, kv->tmap, l,
                                       max_ctx, attn_out, m->ctx->exp_table, m->status, st);
       else if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx))
@@ -397,6 +405,7 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
 
 // Name of the attention kernel run_forward launches for T tokens (same tests).
 const char* attention_kernel_name(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  if (use_exact_attention(m, T) && use_x4_attention(m, kv, max_ctx)) return "attn_qk_softmax_kernel+attn_pv_kernel";
   if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx)) return "paged_attention_exact3_kernel";
   if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx)) return "paged_attention_exact2_kernel";
   if (use_exact_attention(m, T)) return "paged_attention_exact_kernel";
@@ -455,6 +464,10 @@ int prepare_batch(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t n_seqs, const
     m->h_meta[2 * m->Tmax + i] = (int32_t)(t - 1);
     max_ctx = std::max<int>(max_ctx, (int)end);
   }
+  // attention CTAs start in this order: the longest contexts first
+  int32_t* order = m->h_meta + 3 * m->Tmax;
+  for (size_t i = 0; i < T; ++i) order[i] = (int32_t)i;
+  std::stable_sort(order, order + T, [&](int32_t a, int32_t b) { return m->h_meta[a] > m->h_meta[b]; });
   *T_out = (int)T;
   *max_ctx_out = max_ctx;
   return BITNET_OK;
@@ -464,6 +477,7 @@ int upload_meta(bitnet_cuda_model* m, int T, int n_out, cudaStream_t st) {
   BN_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_meta, T * 4, cudaMemcpyHostToDevice, st));
   BN_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_meta + m->Tmax, T * 4, cudaMemcpyHostToDevice, st));
   BN_CUDA(cudaMemcpyAsync(m->last_row, m->h_meta + 2 * m->Tmax, n_out * 4, cudaMemcpyHostToDevice, st));
+  BN_CUDA(cudaMemcpyAsync(m->order, m->h_meta + 3 * m->Tmax, T * 4, cudaMemcpyHostToDevice, st));
   return BITNET_OK;
 }
 
@@ -483,7 +497,8 @@ void drop_graphs(bitnet_cuda_model* m) {
 
 int ensure_partial(bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
   size_t floats = use_exact_attention(m, T)
-                      ? ((use_exact3_attention(m, kv, max_ctx) || use_exact2_attention(m, kv, max_ctx) ||
+                      ? (use_x4_attention(m, kv, max_ctx) ? attn_x4_scratch_floats(T, m->nkv, max_ctx)
+                         : (use_exact3_attention(m, kv, max_ctx) || use_exact2_attention(m, kv, max_ctx) ||
                           exact_scores_in_smem(m, max_ctx))
                              ? 0
                              : (size_t)T * m->nh * max_ctx)
@@ -656,6 +671,14 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
       m->exact3_smem_max = smem;
     }
   }
+  {
+    const int max_ctx = (int)round_up(cfg->max_position_embeddings, kPage);
+    size_t smem = attn_x4_smem(max_ctx);
+    if (smem <= kExactMaxSmem && attn_x4_prepare(max_ctx) == 0) {
+      m->x4_ok = true;
+      m->x4_smem_max = smem;
+    }
+  }
   // RoPE table for every position the model accepts (rope.rs:100-147).
   std::vector<float> cs, sn;
   if ((rc = build_rope_host(cfg->max_position_embeddings, m->hd, cfg->rope_theta, cs, sn))) return fail(rc);
@@ -680,6 +703,7 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
   if ((rc = m->alloc(&m->tok_pos, T))) return fail(rc);
   if ((rc = m->alloc(&m->tok_seq, T))) return fail(rc);
   if ((rc = m->alloc(&m->last_row, T))) return fail(rc);
+  if ((rc = m->alloc(&m->order, T))) return fail(rc);
   if ((rc = m->alloc(&m->status, 16))) return fail(rc);
   if (tp) {
     const size_t wide = (size_t)std::max(m->qd_all, m->F_all);
@@ -688,7 +712,7 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
     if ((rc = m->alloc(&m->tp_acc, T * H))) return fail(rc);
     if ((rc = m->alloc(&m->tp_rowsum, T))) return fail(rc);
   }
-  cudaError_t e = cudaMallocHost(&m->h_meta, 3 * T * sizeof(int32_t));
+  cudaError_t e = cudaMallocHost(&m->h_meta, 4 * T * sizeof(int32_t));
   if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
   e = cudaMallocHost(&m->h_tokens, T * sizeof(uint32_t));
   if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));

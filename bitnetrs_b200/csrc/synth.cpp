@@ -41,6 +41,23 @@ inline float normal_at(uint64_t key, uint64_t i) {
   return (i & 1) ? r * std::sin(t) : r * std::cos(t);
 }
 
+// Elements [b, e) of the same sequence as normal_at, scaled by stdev, with
+// the radius of each pair computed once (same values, half the logarithms).
+inline void normals_into(uint64_t key, uint64_t b, uint64_t e, float stdev, float* out) {
+  uint64_t i = b;
+  if (i < e && (i & 1)) *out++ = stdev * normal_at(key, i++);
+  for (; i + 1 < e; i += 2) {
+    uint64_t a = mix64(key + (i >> 1) * kGolden);
+    float u1 = (float)((a >> 40) + 1) * (1.0f / 16777216.0f);
+    float u2 = (float)(a & 0xffffffu) * (1.0f / 16777216.0f);
+    float r = std::sqrt(-2.0f * std::log(u1));
+    float t = 6.28318530717958647692f * u2;
+    *out++ = stdev * (r * std::cos(t));
+    *out++ = stdev * (r * std::sin(t));
+  }
+  if (i < e) *out = stdev * normal_at(key, i);
+}
+
 int g_threads = 0;
 
 int nthreads() {
@@ -48,9 +65,11 @@ int nthreads() {
   return std::max(1, n);
 }
 
+// Runs f(b, e) over [0, n) split across threads; `cost` is the work of one
+// item in elements, so row loops spread over threads like element loops.
 template <class F>
-void par(size_t n, F f) {
-  int nt = (int)std::min<size_t>((size_t)nthreads(), std::max<size_t>(1, n / 65536));
+void par(size_t n, F f, size_t cost = 1) {
+  int nt = (int)std::min<size_t>((size_t)nthreads(), std::max<size_t>(1, n * cost / 65536));
   if (nt <= 1) {
     f(0, n);
     return;
@@ -90,9 +109,7 @@ int synth_set_threads(int n) {
 // out[i] = (float)(std * N(0,1)_{offset+i}) of stream (seed, stream).
 void synth_normal_f32(uint64_t seed, uint64_t stream, uint64_t offset, size_t n, float stdev, float* out) {
   uint64_t key = stream_key(seed, stream);
-  par(n, [&](size_t b, size_t e) {
-    for (size_t i = b; i < e; ++i) out[i] = stdev * normal_at(key, offset + i);
-  });
+  par(n, [&](size_t b, size_t e) { normals_into(key, offset + b, offset + e, stdev, out + b); });
 }
 
 void synth_bf16_normal(uint64_t seed, uint64_t stream, size_t n, float stdev, uint16_t* out) {
@@ -128,7 +145,7 @@ int synth_ternary_absmean(uint64_t seed, uint64_t stream, size_t rows, size_t co
         dst[c / 4] |= (uint8_t)(bits << (2 * (c % 4)));
       }
     }
-  });
+  }, cols);
   *scale_out = scale;
   return 0;
 }
@@ -148,7 +165,7 @@ void synth_ternary_codes(uint64_t seed, uint64_t stream, size_t rows, size_t col
         dst[c / 4] |= (uint8_t)(bits << (2 * (c % 4)));
       }
     }
-  });
+  }, cols);
 }
 
 // loader.rs:297-340 (quantize_bf16_rows_to_i8).
@@ -170,7 +187,7 @@ void synth_quantize_bf16_rows_to_i8(const uint16_t* bf, size_t rows, size_t row_
         out[r * row_len + i] = (int8_t)q;
       }
     }
-  });
+  }, row_len);
 }
 
 // Uniform integers in [lo, hi] (inclusive).
@@ -193,10 +210,10 @@ void synth_kv_normal(uint64_t seed, uint32_t seq, uint32_t layers, uint32_t kv_h
           uint64_t key = mix64(seed ^ mix64(((uint64_t)seq << 40) ^ ((uint64_t)layer << 24) ^ ((uint64_t)kind << 20) ^
                                              ((uint64_t)h << 16) ^ 0x5eedULL));
           float* dst = (kind == 0 ? k : v) + (lp * kv_heads + h) * hd;
-          for (uint32_t d = 0; d < hd; ++d) dst[d] = normal_at(key, (uint64_t)pos * hd + d);
+          normals_into(key, (uint64_t)pos * hd, (uint64_t)pos * hd + hd, 1.0f, dst);
         }
     }
-  });
+  }, (size_t)2 * kv_heads * hd);
 }
 
 }  // extern "C"

@@ -32,6 +32,26 @@ def shard_requests(ctx_lens: Sequence[int], world: int) -> List[List[int]]:
     return [sorted(s) for s in out]
 
 
+def shard_requests_equal(ctx_lens: Sequence[int], world: int, per_rank: int) -> List[List[int]]:
+    """Split `world * per_rank` requests into `world` sets of exactly
+    `per_rank`, balancing sum(ctx_len + 1) with the same longest-first greedy
+    rule as :func:`shard_requests`, restricted to ranks that still have room.
+    This is the placement for a fixed batch per GPU (weak scaling): every
+    rank decodes the same number of sequences and about the same KV bytes."""
+    if world < 1 or per_rank < 0:
+        raise ValueError("world must be >= 1 and per_rank >= 0")
+    if len(ctx_lens) != world * per_rank:
+        raise ValueError("expected world * per_rank requests")
+    order = sorted(range(len(ctx_lens)), key=lambda i: (-(int(ctx_lens[i]) + 1), i))
+    load = [0] * world
+    out: List[List[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min((k for k in range(world) if len(out[k]) < per_rank), key=lambda k: (load[k], k))
+        out[r].append(i)
+        load[r] += int(ctx_lens[i]) + 1
+    return [sorted(s) for s in out]
+
+
 def shard_loads(ctx_lens: Sequence[int], shards: List[List[int]]) -> List[int]:
     """KV positions each rank reads per decode step."""
     return [sum(int(ctx_lens[i]) + 1 for i in s) for s in shards]

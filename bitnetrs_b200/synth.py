@@ -94,6 +94,34 @@ def random_model(cfg: ModelConfig, seed: int = 0, std: float = 0.02, norm_gain: 
     return ModelWeights(cfg, embed, lm_i8, lm_s, np.full(H, norm_gain, dtype=np.float32), layers)
 
 
+# absmean ternarisation of N(0, s) weights zeroes |w| < 0.5 * E|w| = 0.5 *
+# sqrt(2/pi) * s: P(0) = 2 * Phi(0.5 * sqrt(2/pi)) - 1, and the scale is E|w|.
+ABSMEAN_P_ZERO = 0.3100643
+ABSMEAN_SCALE_PER_STD = 0.7978846
+
+
+def random_model_iid(cfg: ModelConfig, seed: int = 0, std: float = 0.02, norm_gain: float = 1.0) -> ModelWeights:
+    """Random-init model whose ternary codes are drawn directly from the
+    distribution absmean ternarisation of N(0, std) weights produces (P(0) =
+    0.310, P(+1) = P(-1) = 0.345, per-tensor scale std * sqrt(2/pi)) instead
+    of ternarising drawn weights: the same distributions and formats as
+    :func:`random_model` at a fraction of the host time, for benchmark
+    shapes whose exact values no test compares."""
+    H, F, V, qd, kvd = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size, cfg.q_dim(), cfg.kv_dim()
+    p_pm = (1.0 - ABSMEAN_P_ZERO) / 2.0
+    scale = float(np.float32(std * ABSMEAN_SCALE_PER_STD))
+    layers = []
+    for l in range(cfg.num_hidden_layers):
+        base = 1000 + 16 * l
+        shapes = [(qd, H), (kvd, H), (kvd, H), (H, qd), (F, H), (F, H), (H, F)]
+        t = [ternary_codes(seed, base + j, r, c, p_pm, ABSMEAN_P_ZERO) for j, (r, c) in enumerate(shapes)]
+        ones = lambda n: np.full(n, norm_gain, dtype=np.float32)  # noqa: E731
+        layers.append(LayerWeights(*t, *([scale] * 7), ones(H), ones(qd), ones(H), ones(F)))
+    embed = bf16_normal(seed, 1, V * H, std)
+    lm_i8, lm_s = quantize_bf16_rows_to_i8(embed, V, H)
+    return ModelWeights(cfg, embed, lm_i8, lm_s, np.full(H, norm_gain, dtype=np.float32), layers)
+
+
 def tiny_reference_model(cfg: ModelConfig) -> ModelWeights:
     """The reference's golden tiny model (model/src/lib.rs:1459-1545): all-zero
     ternary projections (0x55 bytes, scale 1.0), unit norms, embedding

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 import oracle_lib as O
-from bitnetrs_b200 import KV_BF16, KV_F32, BitNetModel, ModelConfig, bitnet_2b_config, tiny_config
+from bitnetrs_b200 import KV_BF16, KV_F32, BitNetModel, ModelConfig, tiny_config
 from bitnetrs_b200 import synth
 from kat_runner import by_fn
 
@@ -310,7 +310,7 @@ def test_reference_order_decode_bf16_hd128(cuda_backend, gqa4_2kv):
     ctx = [synth.kv_normal(71, s, cfg, n) for s, n in zip(seqs, X3_LENS)]
     for s, (k, v) in zip(seqs, ctx):
         kv.write(s, k, v)
-    assert m.attention_kernel(kv, len(seqs)) == "paged_attention_exact3_kernel"
+    assert m.attention_kernel(kv, len(seqs)) == "attn_qk_softmax_kernel+attn_pv_kernel"
     toks = synth.uniform_u32(3, 3, len(seqs), 0, cfg.vocab_size - 1).tolist()
     for step in range(2):
         nxt, logits = m.decode_step(kv, seqs, toks, want_logits=True)
@@ -334,7 +334,7 @@ def test_reference_order_prefill_bf16_hd128(cuda_backend, gqa4_2kv):
     om = O.OracleModel(w)
     okv = om.kv(cfg.max_position_embeddings, bf16=True)
     toks = synth.uniform_u32(13, 5, 203, 0, cfg.vocab_size - 1).tolist()
-    assert m.attention_kernel(kv, 200) == "paged_attention_exact3_kernel"
+    assert m.attention_kernel(kv, 200) == "attn_qk_softmax_kernel+attn_pv_kernel"
     np.testing.assert_array_equal(m.forward(toks[:200], 0, kv), om.forward(okv, toks[:200], 0))
     for i in range(200, 203):
         np.testing.assert_array_equal(m.forward([toks[i]], i, kv), om.forward(okv, [toks[i]], i))
@@ -369,42 +369,3 @@ def _raise_invalid_config(backend):
     layers = (N.LayerWeights * 1)()
     wts = N.Weights(None, None, None, None, layers)
     N.check(N.cuda_lib().bitnet_cuda_model_create(backend.handle, C.byref(cfg), C.byref(wts), 8, C.byref(h)))
-
-
-@pytest.mark.parametrize("kv_dtype", [KV_F32, KV_BF16], ids=["f32kv", "bf16kv"])
-def test_2b_greedy_decode_token_identical(cuda_backend, kv_dtype):
-    """The 2B architecture, random init, 128-token seeded
-    prompt, 128 greedy tokens at batch 1.  The oracle decodes greedily; the
-    GPU is fed the same tokens (teacher forcing) so every step's logits are
-    compared on identical inputs: logits within the north-star 1e-2 relative
-    at every step and the greedy token identical at every step."""
-    cfg = bitnet_2b_config()
-    w = synth.random_model(cfg, seed=0)
-    prompt = synth.uniform_u32(0, 2, 128, 0, cfg.vocab_size - 1).tolist()
-    m = BitNetModel(w, cuda_backend, max_batch_tokens=256)
-    kv = m.new_kv_cache(num_pages=32, kv_dtype=kv_dtype)
-    om = O.OracleModel(w)
-    okv = om.kv(cfg.max_position_embeddings, bf16=(kv_dtype == KV_BF16))
-    L = O.lib()
-    g = m.forward(prompt, 0, kv)
-    r = om.forward(okv, prompt, 0)
-    stats = []
-    for step in range(128):
-        tok = int(L.orc_greedy_argmax(O.p(r), r.size))
-        top2 = np.partition(r, -2)[-2:]
-        margin = float(top2[1] - top2[0])
-        err = float(np.max(np.abs(g - r)))
-        gtok = int(cuda_backend.greedy_argmax(g))
-        stats.append((step, err, margin, tok, gtok))
-        pos = len(prompt) + step
-        g = m.forward([tok], pos, kv)
-        r = om.forward(okv, [tok], pos)
-    errs = np.array([s[1] for s in stats])
-    bad = [s for s in stats if s[3] != s[4]]
-    print(f"max |dlogit| {errs.max():.3g} (median {np.median(errs):.3g}); bit-identical steps "
-          f"{int(np.sum(errs == 0))}/128; min oracle top-2 margin {min(s[2] for s in stats):.3g}; "
-          f"token mismatches {bad}")
-    assert errs.max() <= 1e-2 * float(np.max(np.abs(r)))
-    assert not bad, f"greedy token differs at {bad[:3]} (step, |dlogit|, oracle top-2 margin, ref, gpu)"
-    # every op reproduces the reference, so the logits are bit-identical
-    assert int(np.sum(errs == 0)) == 128

@@ -18,6 +18,23 @@ import torch.multiprocessing as mp
 from bitnetrs_b200 import ModelConfig, dp, synth
 
 
+def test_shard_requests_equal_counts_and_balance():
+    import numpy as np
+
+    rng = np.random.default_rng(3)
+    for world in (1, 2, 4, 8):
+        ctx = rng.integers(128, 4097, size=256 * world).tolist()
+        shards = dp.shard_requests_equal(ctx, world, 256)
+        assert sorted(i for s in shards for i in s) == list(range(len(ctx)))
+        assert all(len(s) == 256 for s in shards)
+        loads = dp.shard_loads(ctx, shards)
+        assert max(loads) - min(loads) <= max(ctx) + 1
+        assert dp.shard_requests_equal(ctx, world, 256) == shards
+    assert dp.shard_requests_equal(list(range(6)), 1, 6) == [list(range(6))]
+    with pytest.raises(ValueError):
+        dp.shard_requests_equal([1, 2, 3], 2, 2)
+
+
 def test_shard_requests_partition_and_balance():
     ctx = synth.uniform_u32(3, 11, 256, 128, 4096).astype(np.int64)
     for world in (1, 2, 4, 8):
