@@ -16,11 +16,13 @@
 //
 // attn_qk_softmax_kernel (one CTA per (token, kv head), 4 compute warps + a
 //   loader warp, three CTAs per SM): K pages stream through a 16-slot ring of
-//   4 KiB TMA tiles (one page of one kv head, 128-byte swizzle).  Every lane
-//   owns two positions and runs all 32 chains (8 per head) of each, so one
-//   broadcast load of q serves 64 positions and each K element is converted
-//   once for four FMAs.  Raw scores go to a global scratch row [cap][4].  The
-//   same CTA then finishes the softmax: max from the lanes' running maxima,
+//   4 KiB TMA tiles (one page of one kv head, 128-byte swizzle) that holds two
+//   rounds of every warp's pages, so a warp's next pages land while it
+//   computes.  Every lane owns one position and runs all 32 chains (8 per
+//   head) of it, so one broadcast load of q serves 32 positions and each K
+//   element is converted once for four FMAs.  Raw scores go to a global
+//   scratch row [cap][4].  The same CTA then finishes the softmax: max from
+//   the lanes' running maxima,
 //   e = exp(x - m) into shared memory (the ring, reused), the four serial sums
 //   (one thread per head, reference order), and p = e * (1/sum) written back
 //   over the scores.
@@ -47,8 +49,8 @@ namespace {
 constexpr int kSlotBytes = 4096;                         // one page of one kv head: [16 rows][2 halves][64] bf16
 constexpr int kQkWarps = 4;                              // compute warps of the QK kernel
 constexpr int kQkThreads = (kQkWarps + 1) * 32;          // + the loader warp
-constexpr int kQkSlots = 16;                             // ring pages: one round (4 warps x 4 pages)
-constexpr int kQkRound = kQkSlots * kPage;               // positions per round (256)
+constexpr int kQkSlots = 16;                             // ring pages: two rounds of the four warps
+constexpr int kQkRoundPages = 2 * kQkWarps;              // pages per round: two per warp (one row per lane)
 constexpr int kEChunk = kQkSlots * kSlotBytes / 16;      // exp values (float4 per position) the ring holds
 constexpr int kPvWarps = 2;                              // PV warps
 constexpr int kPvThreads = (kPvWarps + 1) * 32;          // + the loader warp
@@ -142,7 +144,7 @@ __device__ __forceinline__ void give_up(volatile int* abort_flag, int32_t* statu
 
 }  // namespace
 
-// One CTA per (token order[blockIdx.x], kv head blockIdx.y): the scores of the
+// One CTA per (token order[blockIdx.x / kv_heads], kv head blockIdx.x % kv_heads): the scores of the
 // group's four heads over the token's context, then its softmax; p[t][pos]
 // (float4 over the four heads) is left in sp[(t * kv_heads + kvh) * cap + pos].
 __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
   __shared__ int last_page[kQkSlots];  // last page issued into each slot (-1: none)
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kvh = blockIdx.y;
+  const int kvh = (int)(blockIdx.x % (unsigned)g.kv_heads), oi = (int)(blockIdx.x / (unsigned)g.kv_heads);
   pdl_launch_dependents();
   pdl_wait();
   q = after_wait(q);
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
   tok_seq = after_wait(tok_seq);
   order = after_wait(order);
   page_table = after_wait(page_table);
-  const int t = order ? order[blockIdx.x] : (int)blockIdx.x;
+  const int t = order ? order[oi] : oi;
   const int ctx = tok_pos[t] + 1;
   if (ctx > cap || ctx <= 0) {  // uniform over the block
     if (tid == 0) atomicOr(status, kStatusBadContext);
@@ -210,9 +212,9 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
     if (lane < i) issue(lane);
     // page k reuses the slot of page k - kQkSlots once its warp has read it
     // (the slot's empty barrier completes phase k / kQkSlots - 1); a warp
-    // frees its four pages together, so they are refilled four at a time
+    // frees its two pages together, so they are refilled two at a time
     while (i < n && !*abort_p) {
-      const int nb = min(4, n - i);
+      const int nb = min(2, n - i);
       if (lane < nb) {
         const int k = i + lane;
         if (mbar_wait(smem_u32(&empty_bar[k % kQkSlots]), ((k / kQkSlots) - 1) & 1, abort_p))
@@ -225,74 +227,59 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
     }
     if (lane < 4) red[kQkWarps][lane] = -INFINITY;
   } else {
-    // ---------------- QK: warp w reads pages 16j + 4w .. 16j + 4w + 3 of round j ----------------
+    // ---------------- QK: warp w reads pages 8j + 2w and 8j + 2w + 1 of round j ----------------
+    // The ring holds two rounds, so a warp's next pages land while it
+    // computes; lane l owns row l & 15 of page 8j + 2w + (l >> 4).
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
     const uint32_t ring_s = smem_u32(ring), qs_s = smem_u32(qs);
-    const int r = lane & 15, hp = lane >> 4;  // row in the page; which page of each pair
+    const int r = lane & 15, hp = lane >> 4;
     // 16-byte chunk c of row r sits in 128-byte unit u = 2r + (c >> 3) at
     // chunk (c & 7) ^ (u & 7); a unit's base has no bits in 4..6, so the
     // address is (base_u | ((u & 7) << 4)) ^ ((c & 7) << 4)
     const uint32_t xo0 = (uint32_t)((2 * r) & 7) << 4, xo1 = (uint32_t)((2 * r + 1) & 7) << 4;
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    for (int p0 = warp * 4; p0 < n; p0 += kQkSlots) {
-      bool ok = true;
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (p0 + k < n && ok) ok = mbar_wait(smem_u32(&full_bar[(p0 + k) % kQkSlots]), ((p0 + k) / kQkSlots) & 1,
-                                             abort_p);
+    for (int p0 = warp * 2; p0 < n; p0 += kQkRoundPages) {
+      bool ok = mbar_wait(smem_u32(&full_bar[p0 % kQkSlots]), (p0 / kQkSlots) & 1, abort_p);
+      if (ok && p0 + 1 < n) ok = mbar_wait(smem_u32(&full_bar[(p0 + 1) % kQkSlots]), ((p0 + 1) / kQkSlots) & 1, abort_p);
       if (!ok) {
         give_up(abort_p, status);
         break;
       }
-      const int pa = p0 + hp, pb = p0 + 2 + hp;  // pages of this lane's positions A and B
+      const int pa = p0 + hp;  // this lane's page (past the context when pa >= n: not loaded, masked)
       const uint32_t ba = ring_s + (uint32_t)(pa % kQkSlots) * kSlotBytes + (uint32_t)(2 * r) * 128;
-      const uint32_t bb = ring_s + (uint32_t)(pb % kQkSlots) * kSlotBytes + (uint32_t)(2 * r) * 128;
-      const uint32_t ca0 = ba | xo0, ca1 = (ba + 128) | xo1, cb0 = bb | xo0, cb1 = (bb + 128) | xo1;
-      float acc[2][4][8];
+      const uint32_t c0 = ba | xo0, c1 = (ba + 128) | xo1;
+      float acc[4][8];
 #pragma unroll
-      for (int a = 0; a < 2; ++a)
+      for (int h = 0; h < 4; ++h)
 #pragma unroll
-        for (int h = 0; h < 4; ++h)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[a][h][j] = 0.0f;
+        for (int j = 0; j < 8; ++j) acc[h][j] = 0.0f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        const uint32_t sw = (uint32_t)(c & 7) << 4;
-        const uint4 ka = lds128((c < 8 ? ca0 : ca1) ^ sw);
-        const uint4 kb = lds128((c < 8 ? cb0 : cb1) ^ sw);
-        const float fa[8] = {bf_lo(ka.x), bf_hi(ka.x), bf_lo(ka.y), bf_hi(ka.y),
-                             bf_lo(ka.z), bf_hi(ka.z), bf_lo(ka.w), bf_hi(ka.w)};
-        const float fb[8] = {bf_lo(kb.x), bf_hi(kb.x), bf_lo(kb.y), bf_hi(kb.y),
-                             bf_lo(kb.z), bf_hi(kb.z), bf_lo(kb.w), bf_hi(kb.w)};
+        const uint4 k4 = lds128((c < 8 ? c0 : c1) ^ ((uint32_t)(c & 7) << 4));
+        const float kf[8] = {bf_lo(k4.x), bf_hi(k4.x), bf_lo(k4.y), bf_hi(k4.y),
+                             bf_lo(k4.z), bf_hi(k4.z), bf_lo(k4.w), bf_hi(k4.w)};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           const float4 q0 = lds128f(qs_s + (uint32_t)(h * 128 + 8 * c) * 4);
           const float4 q1 = lds128f(qs_s + (uint32_t)(h * 128 + 8 * c + 4) * 4);
           const float qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            acc[0][h][j] = __fmaf_rn(qq[j], fa[j], acc[0][h][j]);
-            acc[1][h][j] = __fmaf_rn(qq[j], fb[j], acc[1][h][j]);
-          }
+          for (int j = 0; j < 8; ++j) acc[h][j] = __fmaf_rn(qq[j], kf[j], acc[h][j]);
         }
       }
       __syncwarp();
       if (lane == 0) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (p0 + k < n) mbar_arrive(smem_u32(&empty_bar[(p0 + k) % kQkSlots]));
+        mbar_arrive(smem_u32(&empty_bar[p0 % kQkSlots]));
+        if (p0 + 1 < n) mbar_arrive(smem_u32(&empty_bar[(p0 + 1) % kQkSlots]));
       }
+      const int pos = pa * kPage + r;
+      float sc[4];
 #pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        const int pos = (a ? pb : pa) * kPage + r;
-        float sc[4];
+      for (int h = 0; h < 4; ++h) sc[h] = __fmul_rn(hsum8(acc[h]), scale);
+      if (pos < ctx) {
+        sp[row + pos] = make_float4(sc[0], sc[1], sc[2], sc[3]);
 #pragma unroll
-        for (int h = 0; h < 4; ++h) sc[h] = __fmul_rn(hsum8(acc[a][h]), scale);
-        if (pos < ctx) {
-          sp[row + pos] = make_float4(sc[0], sc[1], sc[2], sc[3]);
-#pragma unroll
-          for (int h = 0; h < 4; ++h) mx[h] = fmaxf(mx[h], sc[h]);
-        }
+        for (int h = 0; h < 4; ++h) mx[h] = fmaxf(mx[h], sc[h]);
       }
     }
 #pragma unroll
@@ -361,7 +348,7 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
   }
 }
 
-// One CTA per (token order[blockIdx.x], kv head blockIdx.y): out = sum_t p_t V_t
+// One CTA per (token order[blockIdx.x / kv_heads], kv head blockIdx.x % kv_heads): out = sum_t p_t V_t
 // for the group's four heads, p from the QK kernel's rows of sp.
 __global__ void __launch_bounds__(kPvThreads, 6) attn_pv_kernel(
     const int32_t* __restrict__ tok_pos, const int32_t* __restrict__ tok_seq, const int32_t* __restrict__ order,
@@ -373,7 +360,7 @@ __global__ void __launch_bounds__(kPvThreads, 6) attn_pv_kernel(
   __shared__ int last_page[kPvSlots];
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kvh = blockIdx.y;
+  const int kvh = (int)(blockIdx.x % (unsigned)g.kv_heads), oi = (int)(blockIdx.x / (unsigned)g.kv_heads);
   pdl_launch_dependents();
   pdl_wait();
   tok_pos = after_wait(tok_pos);
@@ -381,7 +368,7 @@ __global__ void __launch_bounds__(kPvThreads, 6) attn_pv_kernel(
   order = after_wait(order);
   page_table = after_wait(page_table);
   sp = after_wait(sp);
-  const int t = order ? order[blockIdx.x] : (int)blockIdx.x;
+  const int t = order ? order[oi] : oi;
   const int ctx = tok_pos[t] + 1;
   if (ctx > cap || ctx <= 0) {
     if (tid == 0) atomicOr(status, kStatusBadContext);
@@ -549,11 +536,11 @@ void launch_attn_x4(const float* q, int T, int nh, const int32_t* tok_pos, const
   if (T <= 0) return;
   const int cap = attn_x4_cap(max_ctx);
   float4* sp = reinterpret_cast<float4*>(scratch);
-  attn_qk_softmax_kernel<<<dim3(T, kv.kv_heads), kQkThreads, qk_smem(cap), st>>>(q, nh, tok_pos, tok_seq, order,
+  attn_qk_softmax_kernel<<<(unsigned)(T * kv.kv_heads), kQkThreads, qk_smem(cap), st>>>(q, nh, tok_pos, tok_seq, order,
                                                                                  page_table, kv, layer, cap, sp, et,
                                                                                  status, map);
   count_launch();
-  attn_pv_kernel<<<dim3(T, kv.kv_heads), kPvThreads, pv_smem(cap), st>>>(tok_pos, tok_seq, order, page_table, kv,
+  attn_pv_kernel<<<(unsigned)(T * kv.kv_heads), kPvThreads, pv_smem(cap), st>>>(tok_pos, tok_seq, order, page_table, kv,
                                                                          layer, cap, nh, sp, out, status, map);
   count_launch();
 }

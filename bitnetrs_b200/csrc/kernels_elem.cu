@@ -505,10 +505,10 @@ __global__ void exp_candidates_kernel(uint32_t lo, uint32_t hi, uint2* out, uint
        i += (uint64_t)gridDim.x * blockDim.x) {
     uint32_t u = lo + (uint32_t)i;
     float x = __uint_as_float(u);
-    double d = exp((double)x);
+    double d = exp_f64(x);
     float f = (float)d;
     if (!(f > 0.0f) || isinf(f)) continue;
-    if (exp_round_position(d, f) > 0.497) {
+    if (exp_near_midpoint(d, f)) {
       uint32_t slot = atomicAdd(count, 1u);
       if (slot < cap) out[slot] = make_uint2(u, __float_as_uint(f));
     }

@@ -196,10 +196,15 @@ int bitnet_cuda_ternary_matmul_device(bitnet_cuda_ctx* ctx, const bitnet_cuda_we
  * call resets the scratch's flag itself; nothing has to start at zero.
  *  - The first call on a device resolves the scratch's address; make it
  *    before any stream capture on that device.
+ *  - The resolved address is kept for the life of the process: do not use
+ *    this entry point across a cudaDeviceReset (or a reset of the primary
+ *    context) of that device.
  *  - All calls on one device share the scratch: calls that overlap in time
  *    (other threads, or other streams still running) race; serialise them.
  *  - Runs on `stream` (NULL = the context's stream) and returns after the
- *    result is in `out`; a non-finite x returns QuantizationError. */
+ *    result is in `out`; a non-finite x returns QuantizationError, and `out`
+ *    is then unspecified (the product has already run on the clamped codes),
+ *    unlike the allocating path, which returns before touching `out`. */
 int bitnet_cuda_ternary_gemv_quant_noalloc(bitnet_cuda_ctx* ctx, const bitnet_cuda_weight* w, const float* x,
                                            size_t x_len, float* out, size_t out_len, void* stream);
 
