@@ -90,18 +90,43 @@ int build_rope_host(size_t max_seq, size_t head_dim, float theta, std::vector<fl
   return BITNET_OK;
 }
 
-// The host libm's expf on every x in [-112, -0] whose exp evaluated in
-// double lands within 0.003 ulp of a float rounding midpoint (the GPU
-// enumerates them), kept where it differs from the double-rounded value.
+// The host libm's expf on every x in [-112, -0] whose device exp
+// (exp_candidate) lands within 0.003 ulp of a float rounding midpoint (the
+// GPU enumerates them), kept where it differs from the device's value.  The
+// pair tables of exp_pair are computed here first, in long double.
 int ensure_exp_table(bitnet_cuda_ctx* c) {
   if (c->exp_ready) return BITNET_OK;
+  {
+    std::vector<float4> en(88);
+    for (int k = 0; k < 88; ++k) {
+      const long double v = expl(-(long double)k);
+      const int S = (int)lrintl((long double)k * 1.442695040888963407359924681L);  // k / ln 2
+      const long double w = ldexpl(v, S);
+      const float h = (float)w;
+      float sbits;
+      std::memcpy(&sbits, &S, 4);
+      en[k] = make_float4(h, (float)(w - (long double)h), sbits, 0.0f);
+    }
+    std::vector<float2> fj(128);
+    for (int j = 0; j < 128; ++j) {
+      const long double v = expl(-(long double)j / 128.0L);
+      const float h = (float)v;
+      fj[j] = make_float2(h, (float)(v - (long double)h));
+    }
+    BN_TRY(c->exp_en.ensure(en.size() * sizeof(float4)));
+    BN_TRY(c->exp_fj.ensure(fj.size() * sizeof(float2)));
+    BN_CUDA(cudaMemcpy(c->exp_en.p, en.data(), en.size() * sizeof(float4), cudaMemcpyHostToDevice));
+    BN_CUDA(cudaMemcpy(c->exp_fj.p, fj.data(), fj.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    c->exp_table.en = c->exp_en.as<float4>();
+    c->exp_table.fj = c->exp_fj.as<float2>();
+  }
   const uint32_t lo = 0x80000000u, hi = 0xC2E00000u;  // -0 .. -112
   const uint32_t cap = 8u << 20;
   DevBuf cand, cnt;
   BN_TRY(cand.ensure((size_t)cap * sizeof(uint2)));
   BN_TRY(cnt.ensure(sizeof(uint32_t)));
   BN_CUDA(cudaMemsetAsync(cnt.p, 0, sizeof(uint32_t), c->stream));
-  launch_exp_candidates(lo, hi, cand.as<uint2>(), cap, cnt.as<uint32_t>(), c->stream);
+  launch_exp_candidates(lo, hi, cand.as<uint2>(), cap, cnt.as<uint32_t>(), c->exp_table, c->stream);
   uint32_t n = 0;
   BN_CUDA(cudaMemcpyAsync(&n, cnt.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
   BN_CUDA(cudaStreamSynchronize(c->stream));
@@ -129,30 +154,37 @@ int ensure_exp_table(bitnet_cuda_ctx* c) {
     BN_CUDA(cudaMemcpy(c->exp_keys.p, keys.data(), keys.size() * 4, cudaMemcpyHostToDevice));
     BN_CUDA(cudaMemcpy(c->exp_vals.p, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice));
   }
-  // open-addressing copy: load factor <= 0.4, linear probing
-  uint32_t bits = 10;
-  while ((1u << bits) < keys.size() * 5 / 2) ++bits;
-  const uint32_t slots = 1u << bits;
-  std::vector<uint2> hash(slots, make_uint2(0u, 0u));
-  int probes = 0;
-  for (size_t i = 0; i < keys.size(); ++i) {
-    uint32_t j = (keys[i] * kExpHashMul) >> (32 - bits);
-    int k = 0;
-    while (hash[(j + k) & (slots - 1)].x != 0u) ++k;
-    uint32_t vb;
-    std::memcpy(&vb, &vals[i], 4);
-    hash[(j + k) & (slots - 1)] = make_uint2(keys[i], vb);
-    probes = std::max(probes, k);
+  // two-choice bucketed copy: start at ~2 keys per bucket of 8 and double
+  // the bucket count until every key fits
+  uint32_t bits = 4;
+  while ((1u << bits) * 2 < keys.size()) ++bits;
+  std::vector<uint2> slot;
+  for (;; ++bits) {
+    const uint32_t nb = 1u << bits;
+    slot.assign((size_t)nb * kExpBucketSlots, make_uint2(0u, 0u));
+    std::vector<int> fill(nb, 0);
+    bool ok = true;
+    for (size_t i = 0; i < keys.size() && ok; ++i) {
+      const uint32_t b1 = (keys[i] * kExpHashMul) >> (32 - bits), b2 = (keys[i] * kExpHashMul2) >> (32 - bits);
+      const uint32_t bk = fill[b2] < fill[b1] ? b2 : b1;
+      if (fill[bk] == kExpBucketSlots) {
+        ok = false;
+        break;
+      }
+      uint32_t vb;
+      std::memcpy(&vb, &vals[i], 4);
+      slot[(size_t)bk * kExpBucketSlots + fill[bk]++] = make_uint2(keys[i], vb);
+    }
+    if (ok) break;
+    if (bits >= 24) return backend_error("exp exception table does not fit its buckets");
   }
-  BN_TRY(c->exp_hash.ensure((size_t)slots * sizeof(uint2)));
-  BN_CUDA(cudaMemcpy(c->exp_hash.p, hash.data(), (size_t)slots * sizeof(uint2), cudaMemcpyHostToDevice));
+  BN_TRY(c->exp_hash.ensure(slot.size() * sizeof(uint2)));
+  BN_CUDA(cudaMemcpy(c->exp_hash.p, slot.data(), slot.size() * sizeof(uint2), cudaMemcpyHostToDevice));
   c->exp_table.keys = c->exp_keys.as<uint32_t>();
   c->exp_table.vals = c->exp_vals.as<float>();
   c->exp_table.n = (int)keys.size();
-  c->exp_table.hash = c->exp_hash.as<uint2>();
-  c->exp_table.hash_shift = 32 - bits;
-  c->exp_table.hash_mask = slots - 1;
-  c->exp_table.hash_probes = probes;
+  c->exp_table.buckets = c->exp_hash.as<uint4>();
+  c->exp_table.bucket_shift = 32 - bits;
   c->exp_ready = true;
   return BITNET_OK;
 }
@@ -170,6 +202,8 @@ void ctx_release(bitnet_cuda_ctx* c) {
   c->exp_keys.release();
   c->exp_vals.release();
   c->exp_hash.release();
+  c->exp_en.release();
+  c->exp_fj.release();
   cudaStreamDestroy(c->stream);
   delete c;
 }

@@ -108,29 +108,37 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* smem32) {
 }
 
 // exp for the reference's softmax (ops.rs:206-227), which calls f32::exp ->
-// the host libm's expf.  exp is evaluated in double and rounded to float,
-// which is the correctly rounded result except when the double lands within
-// 2^-20 ulp of a rounding boundary; the host libm itself is within 0.502 ulp
-// of the exact value, so the two can only disagree when the exact value is
-// within 0.002 ulp of a float midpoint.  Inputs whose double result lies that
-// close (|position| > 0.497 ulp from the rounded value, ~0.15% of inputs) are
-// looked up in a table of the host libm's results that differ from the
-// double-rounded one (measured once per device, see ensure_exp_table); all
-// other inputs already agree.  The table covers x in [-112, 0], the range of
-// the softmax's x - max (below -112 both give 0).  It is held twice: sorted
-// (keys/vals, binary search) and as an open-addressing hash of (key, value)
-// pairs (linear probing, at most hash_probes slots per lookup, key 0 = empty
-// since +0.0 is never an entry).
+// the host libm's expf.  The device computes exp far more precisely than a
+// float (exp_pair; exp_f64 outside [-87, 0]) and rounds; that agrees with
+// the host libm except where the exact value lies very close to a float
+// midpoint (the host libm's own disagreements with the correctly rounded
+// value all lie within 0.00165 ulp of one, measured over every float of
+// [-87, 0]).  Inputs whose value lies within 0.003 ulp of a midpoint
+// (position > 0.497 ulp from the rounded value, ~0.15% of inputs) are table
+// candidates; the table holds the host libm's value for each candidate of
+// [-112, -0] where it differs from the device's rounded value (built once
+// per device by ensure_exp_table from the device's own candidates), and
+// every other input already agrees.  Below -112 both give 0.  The table is
+// held sorted (keys/vals, binary search) and as a two-choice bucketed hash:
+// buckets of 8 (key, value bits) slots, 64 bytes each, the key in the less
+// full of buckets h1(key) and h2(key), so a lookup loads both buckets at
+// once (one memory round trip); key 0 marks an empty slot (+0.0 is never a
+// key).
 struct ExpTable {
   const uint32_t* keys = nullptr;  // float bit patterns, ascending
   const float* vals = nullptr;     // the host libm's expf of each key
   int n = 0;
-  const uint2* hash = nullptr;     // (key, value bits) slots
-  uint32_t hash_shift = 32;        // slot = (key * kExpHashMul) >> hash_shift
-  uint32_t hash_mask = 0;          // slots - 1
-  int hash_probes = 0;             // longest probe sequence in the table
+  const uint4* buckets = nullptr;  // [nbuckets][4] uint4 = 8 (key, value bits) slots each
+  uint32_t bucket_shift = 32;      // bucket = (key * multiplier) >> bucket_shift
+  // float-pair tables of exp_pair: en[k] = (hi, lo, S as int bits, 0) with
+  // hi + lo = exp(-k) * 2^S (k < 88, S = round(k / ln2)); fj[j] = (hi, lo) =
+  // exp(-j/128)
+  const float4* en = nullptr;
+  const float2* fj = nullptr;
 };
-constexpr uint32_t kExpHashMul = 0x9E3779B1u;
+constexpr uint32_t kExpHashMul = 0x9E3779B1u;   // h1
+constexpr uint32_t kExpHashMul2 = 0x85EBCA77u;  // h2
+constexpr int kExpBucketSlots = 8;
 
 __device__ __forceinline__ double exp_round_position(double d, float f) {
   uint32_t fb = __float_as_uint(f);
@@ -181,27 +189,98 @@ __device__ __forceinline__ bool exp_near_midpoint(double d, float f) {
   return exp_round_position(d, f) > 0.497;
 }
 
-// First half of exp_host_libm: the double-rounded value, and whether the
-// input needs the table (returns true; the caller resolves it later).
-__device__ __forceinline__ bool exp_needs_table(float x, const ExpTable& t, float* out) {
+// exp for x in [-87, 0] in single-precision pairs (the softmax's x - max),
+// to far better than float precision: the reduction x = n + j/128 + r (n =
+// ceil(x), j = ceil(128 (x - n)), r in (-1/128, 0]) is exact; exp(r) = 1 +
+// r + r^2 (1/2 + r (1/6 + r (1/24 + r/120))) with 1 + r kept as an exact
+// pair; exp(n) (scaled by 2^S into [0.7, 1.4]) and exp(j/128) come from the
+// pair tables; two pair products and a renormalisation give hi + lo, within
+// 1e-4 float ulp of exp(x) * 2^S.  f = hi * 2^-S is the rounded value, and
+// the input is a table candidate when lo lies more than 0.497 ulp from hi
+// (toward lo: the grid below a power of two is twice as fine).  A CPU mirror
+// of these exact operations was checked against the host libm's expf on
+// every float of [-87, 0]: every non-candidate agrees bit for bit.
+// Returns -1 outside [-87, 0] (the caller falls back to exp_f64), else
+// whether x is a candidate, with f in *out.
+__device__ __forceinline__ int exp_pair(float x, const ExpTable& t, float* out) {
+  if (!(x >= -87.0f && x <= 0.0f) || t.en == nullptr) return -1;
+  // ceil(v) for |v| < 2^22: v + 1.5 * 2^23 rounded up is an integer whose
+  // value sits in the low mantissa bits (no conversion instruction needed)
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float nm = __fadd_ru(x, kMagic);
+  const float n = __fsub_rn(nm, kMagic);  // ceil(x)
+  const float fr = __fsub_rn(x, n);
+  const float jm = __fadd_ru(__fmul_rn(fr, 128.0f), kMagic);
+  const float jf = __fsub_rn(jm, kMagic);  // ceil(128 fr)
+  const float r = __fsub_rn(fr, __fmul_rn(jf, 0.0078125f));
+  float q = __fmaf_rn(r, 0x1.111112p-7f, 0x1.555556p-5f);  // 1/120, 1/24
+  q = __fmaf_rn(q, r, 0x1.555556p-3f);                     // 1/6
+  q = __fmaf_rn(q, r, 0.5f);
+  q = __fmul_rn(q, __fmul_rn(r, r));
+  const float a_hi = __fadd_rn(1.0f, r);
+  const float a_lo = __fadd_rn(__fsub_rn(r, __fsub_rn(a_hi, 1.0f)), q);
+  const int k = __float_as_int(kMagic) - __float_as_int(nm);  // -n
+  const int j = __float_as_int(kMagic) - __float_as_int(jm);  // -ceil(128 fr)
+  const float4 E = __ldg(t.en + k);
+  const float2 F = __ldg(t.fj + j);
+  const float p = __fmul_rn(E.x, F.x);
+  float pe = __fmaf_rn(E.x, F.x, -p);
+  pe = __fmaf_rn(E.x, F.y, pe);
+  pe = __fmaf_rn(E.y, F.x, pe);
+  const float y = __fmul_rn(p, a_hi);
+  float ye = __fmaf_rn(p, a_hi, -y);
+  ye = __fmaf_rn(p, a_lo, ye);
+  ye = __fmaf_rn(pe, a_hi, ye);
+  const float hi = __fadd_rn(y, ye);
+  const float lo = __fsub_rn(ye, __fsub_rn(hi, y));
+  const int S = __float_as_int(E.z);
+  const uint32_t hb = __float_as_uint(hi);
+  if ((int)((hb >> 23) & 0xffu) - S <= 0) return -1;  // not reached for x >= -87
+  *out = __uint_as_float(hb - ((uint32_t)S << 23));
+  float ulp = __uint_as_float((hb & 0x7f800000u) - (23u << 23));
+  if (lo < 0.0f && (hb & 0x7fffffu) == 0u) ulp = __fmul_rn(ulp, 0.5f);
+  return fabsf(lo) > __fmul_rn(0.497f, ulp) ? 1 : 0;
+}
+
+// The value exp_host_libm starts from (*out) and whether it lies within
+// 0.003 ulp of a rounding midpoint (a table candidate): exp_pair, or exp_f64
+// outside its range.
+__device__ __forceinline__ bool exp_candidate(float x, const ExpTable& t, float* out) {
+  const int c = exp_pair(x, t, out);
+  if (c >= 0) return c != 0;
   const double d = exp_f64(x);
   const float f = (float)d;
   *out = f;
-  if (t.n == 0 || !(f > 0.0f) || isinf(f)) return false;
+  if (!(f > 0.0f) || isinf(f)) return false;
   return exp_near_midpoint(d, f);
 }
 
+// First half of exp_host_libm: the starting value, and whether the input
+// needs the table (returns true; the caller resolves it later).
+__device__ __forceinline__ bool exp_needs_table(float x, const ExpTable& t, float* out) {
+  const bool c = exp_candidate(x, t, out);
+  return t.n != 0 && c;
+}
+
 // Second half: the host libm's value for a table candidate `key` whose
-// double-rounded value is f.
+// device-rounded value is f.
 __device__ __forceinline__ float exp_table_lookup(uint32_t key, float f, const ExpTable& t) {
-  if (t.hash) {
-    uint32_t i = (key * kExpHashMul) >> t.hash_shift;
-    for (int k = 0; k <= t.hash_probes; ++k) {
-      const uint2 e = t.hash[(i + k) & t.hash_mask];
-      if (e.x == key) return __uint_as_float(e.y);
-      if (e.x == 0u) return f;
+  if (t.buckets) {
+    const uint4* b1 = t.buckets + 4 * (size_t)((key * kExpHashMul) >> t.bucket_shift);
+    const uint4* b2 = t.buckets + 4 * (size_t)((key * kExpHashMul2) >> t.bucket_shift);
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = __ldg(b1 + i);
+      v[4 + i] = __ldg(b2 + i);
     }
-    return f;
+    float r = f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (v[i].x == key) r = __uint_as_float(v[i].y);
+      if (v[i].z == key) r = __uint_as_float(v[i].w);
+    }
+    return r;
   }
   int lo = 0, hi = t.n - 1;
   while (lo <= hi) {

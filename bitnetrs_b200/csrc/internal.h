@@ -53,7 +53,7 @@ struct bitnet_cuda_ctx {
   bitnet::RopeTable rope;
   // host-libm expf exceptions (see ExpTable); built once per context
   bool exp_ready = false;
-  bitnet::DevBuf exp_keys, exp_vals, exp_hash;
+  bitnet::DevBuf exp_keys, exp_vals, exp_hash, exp_en, exp_fj;
   bitnet::ExpTable exp_table;
 };
 

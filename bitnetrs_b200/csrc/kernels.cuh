@@ -201,9 +201,10 @@ void launch_attn_x4(const float* q, int T, int nh, const int32_t* tok_pos, const
                     int layer, int max_ctx, float* out, float* scratch, const ExpTable& et, int32_t* status,
                     cudaStream_t st);
 // Candidates for the exp exception table: bit patterns u in [lo, hi] whose
-// double-evaluated exp lands within 0.003 ulp of a float rounding midpoint;
-// writes (u, (float)exp((double)x)) pairs and counts them in *count.
-void launch_exp_candidates(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count, cudaStream_t st);
+// exp (exp_candidate, with et's pair tables) lands within 0.003 ulp of a
+// float rounding midpoint; writes (u, starting value) pairs and counts them.
+void launch_exp_candidates(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count, const ExpTable& et,
+                           cudaStream_t st);
 
 // Tensor-core decode attention (bf16 cache, head_dim 128, group <= 4), split
 // over the context; partial holds flash_decode_mma_partial_floats floats.

@@ -52,6 +52,7 @@ constexpr int kQkThreads = (kQkWarps + 1) * 32;          // + the loader warp
 constexpr int kQkSlots = 16;                             // ring pages: two rounds of the four warps
 constexpr int kQkRoundPages = 2 * kQkWarps;              // pages per round: two per warp (one row per lane)
 constexpr int kEChunk = kQkSlots * kSlotBytes / 16;      // exp values (float4 per position) the ring holds
+constexpr int kMaxCand = 256;                            // queued host-libm table lookups per chunk (~100 expected)
 constexpr int kPvWarps = 2;                              // PV warps
 constexpr int kPvThreads = (kPvWarps + 1) * 32;          // + the loader warp
 constexpr int kPvSlots = 8;                              // ring pages
@@ -158,7 +159,8 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
   __shared__ float red[kQkWarps + 1][4];
   __shared__ float hstat[4];
   __shared__ int last_page[kQkSlots];  // last page issued into each slot (-1: none)
-  __shared__ int abort_flag;
+  __shared__ uint2 cand[kMaxCand];     // exp inputs that need the host-libm table: (float index in e_sm, x bits)
+  __shared__ int abort_flag, ncand;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = (int)(blockIdx.x % (unsigned)g.kv_heads), oi = (int)(blockIdx.x / (unsigned)g.kv_heads);
   pdl_launch_dependents();
@@ -303,14 +305,39 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
     float sum = 0.0f;  // thread h < 4: the running sum of head h
     for (int c0 = 0; c0 < ctx; c0 += kEChunk) {
       const int len = min(kEChunk, ctx - c0);
+      // e = exp(x - m) of the chunk.  The few inputs whose value needs the
+      // host-libm table are queued and looked up together afterwards (a
+      // lookup is a dependent global load), and each thread's next score row
+      // is loaded while the current one is computed.
+      if (tid == 0) ncand = 0;
+      __syncthreads();
+      float4 xn = tid < len ? sp[row + c0 + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
       for (int i = tid; i < len; i += kQkThreads) {
-        const float4 x = sp[row + c0 + i];
-        const float4 e = make_float4(exp_host_libm(__fsub_rn(x.x, m0), et), exp_host_libm(__fsub_rn(x.y, m1), et),
-                                     exp_host_libm(__fsub_rn(x.z, m2), et), exp_host_libm(__fsub_rn(x.w, m3), et));
-        e_sm[i] = e;
-        if (nchunks > 1) sp[row + c0 + i] = e;
+        const float4 x = xn;
+        if (i + kQkThreads < len) xn = sp[row + c0 + i + kQkThreads];
+        const float xs[4] = {__fsub_rn(x.x, m0), __fsub_rn(x.y, m1), __fsub_rn(x.z, m2), __fsub_rn(x.w, m3)};
+        float e[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          if (exp_needs_table(xs[h], et, &e[h])) {
+            const int k = atomicAdd(&ncand, 1);
+            if (k < kMaxCand)
+              cand[k] = make_uint2((uint32_t)(4 * i + h), __float_as_uint(xs[h]));
+            else
+              e[h] = exp_table_lookup(__float_as_uint(xs[h]), e[h], et);
+          }
+        }
+        e_sm[i] = make_float4(e[0], e[1], e[2], e[3]);
       }
       __syncthreads();
+      {
+        float* ef = reinterpret_cast<float*>(e_sm);
+        const int nc = min(ncand, kMaxCand);
+        for (int k = tid; k < nc; k += kQkThreads) ef[cand[k].x] = exp_table_lookup(cand[k].y, ef[cand[k].x], et);
+      }
+      __syncthreads();
+      if (nchunks > 1)
+        for (int i = tid; i < len; i += kQkThreads) sp[row + c0 + i] = e_sm[i];
       if (tid < 4) {
         // sum = ((e_0 + e_1) + e_2) + ... of head tid, loads issued a block ahead
         const float* e = reinterpret_cast<const float*>(e_sm) + tid;

@@ -500,23 +500,23 @@ void launch_gather_rows(const float* src, int ld, const int32_t* rows, int n, fl
   count_launch();
 }
 
-__global__ void exp_candidates_kernel(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count) {
+__global__ void exp_candidates_kernel(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count,
+                                      ExpTable et) {
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= (uint64_t)(hi - lo);
        i += (uint64_t)gridDim.x * blockDim.x) {
     uint32_t u = lo + (uint32_t)i;
     float x = __uint_as_float(u);
-    double d = exp_f64(x);
-    float f = (float)d;
-    if (!(f > 0.0f) || isinf(f)) continue;
-    if (exp_near_midpoint(d, f)) {
+    float f;
+    if (exp_candidate(x, et, &f)) {
       uint32_t slot = atomicAdd(count, 1u);
       if (slot < cap) out[slot] = make_uint2(u, __float_as_uint(f));
     }
   }
 }
 
-void launch_exp_candidates(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count, cudaStream_t st) {
-  exp_candidates_kernel<<<148 * 16, 256, 0, st>>>(lo, hi, out, cap, count);
+void launch_exp_candidates(uint32_t lo, uint32_t hi, uint2* out, uint32_t cap, uint32_t* count, const ExpTable& et,
+                           cudaStream_t st) {
+  exp_candidates_kernel<<<148 * 16, 256, 0, st>>>(lo, hi, out, cap, count, et);
   count_launch();
 }
 
