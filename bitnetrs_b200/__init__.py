@@ -5,7 +5,7 @@ of ``include/bitnet_cuda.h``).  This package is its Python host mirror:
 
 * :class:`CudaBackend` — the reference ``Backend`` trait (host slices);
 * :class:`BitNetModel` / :class:`KVCache` — device-resident model, paged KV
-  cache, batched decode / prefill, greedy generate;
+  cache, batched decode / prefill, greedy and sampled generate;
 * :mod:`bitnetrs_b200.tp` — tensor-parallel shards over NCCL (one process per GPU);
 * :mod:`bitnetrs_b200.synth` — seeded synthetic models in the reference formats.
 """

@@ -38,6 +38,12 @@ class Config(C.Structure):
     ]
 
 
+class Sampling(C.Structure):
+    """bitnet_cuda_sampling == SamplingConfig (crates/bitnet-inference/src/lib.rs:80-112)."""
+
+    _fields_ = [("temperature", f32), ("top_p", f32), ("top_k", u32), ("repetition_penalty", f32), ("seed", u64)]
+
+
 class LayerWeights(C.Structure):
     """bitnet_cuda_layer_weights == LayerWeights (crates/bitnet-weights/src/loader.rs:121-203)."""
 
@@ -85,6 +91,7 @@ _CUDA_SIGS = {
     "bitnet_cuda_absmax_quantize_row": (i32, [vp, vp, sz, vp, sz, C.POINTER(f32)]),
     "bitnet_cuda_ternary_gemv_preq_acc": (i32, [vp, vp, sz, f32, vp, sz, f32, vp, sz, vp, sz, sz]),
     "bitnet_cuda_greedy_argmax": (i32, [vp, vp, sz, C.POINTER(u32)]),
+    "bitnet_cuda_sample_next_token": (i32, [vp, vp, sz, C.POINTER(Sampling), vp, sz, C.POINTER(u32)]),
     "bitnet_cuda_weight_upload": (i32, [vp, vp, sz, sz, sz, f32, C.POINTER(vp)]),
     "bitnet_cuda_weight_destroy": (None, [vp]),
     "bitnet_cuda_quantize_rows_device": (i32, [vp, vp, i32, sz, sz, vp, sz, vp, vp, vp, vp]),
@@ -111,6 +118,8 @@ _CUDA_SIGS = {
     "bitnet_cuda_decode_step_device": (i32, [vp, vp, sz, vp, vp, vp, vp, vp]),
     "bitnet_cuda_prefill": (i32, [vp, vp, sz, vp, vp, vp, vp, vp]),
     "bitnet_cuda_generate": (i32, [vp, vp, u32, vp, sz, sz, u32, u32, vp, C.POINTER(sz)]),
+    "bitnet_cuda_generate_sampled": (i32, [vp, vp, u32, vp, sz, sz, C.POINTER(Sampling), u32, u32, vp,
+                                           C.POINTER(sz)]),
     "bitnet_cuda_model_check": (i32, [vp]),
     "bitnet_cuda_ternary_gemv_quant_noalloc": (i32, [vp, vp, vp, sz, vp, sz, vp]),
     "bitnet_cuda_model_attention_kernel": (i32, [vp, vp, u32, vp, sz]),

@@ -154,3 +154,15 @@ class CudaBackend:
         t = C.c_uint32()
         check(self._lib.bitnet_cuda_greedy_argmax(self._h, ptr(x), x.size, C.byref(t)))
         return t.value
+
+    def sample_next_token(self, logits: np.ndarray, config, past_tokens=()) -> int:
+        """sample_next_token (crates/bitnet-inference/src/lib.rs:236-390) on the
+        GPU.  `logits` (float32, C-contiguous) is modified in place as the
+        reference modifies it; `config` is a SamplingConfig."""
+        if logits.dtype != np.float32 or not logits.flags.c_contiguous:
+            raise ValueError("logits must be a C-contiguous float32 array")
+        pa = np.ascontiguousarray(np.asarray(past_tokens, dtype=np.uint32))
+        t = C.c_uint32()
+        check(self._lib.bitnet_cuda_sample_next_token(self._h, ptr(logits), logits.size, C.byref(config.to_c()),
+                                                      ptr(pa) if pa.size else None, pa.size, C.byref(t)))
+        return t.value

@@ -202,6 +202,9 @@ void ctx_release(bitnet_cuda_ctx* c) {
   c->exp_keys.release();
   c->exp_vals.release();
   c->exp_hash.release();
+  c->samp_counts.release();
+  c->samp_e.release();
+  c->samp_misc.release();
   c->exp_en.release();
   c->exp_fj.release();
   cudaStreamDestroy(c->stream);
@@ -358,7 +361,7 @@ int bitnet_cuda_create(uint32_t device_id, bitnet_cuda_ctx** out) {
     delete c;
     return rc;
   }
-  if (row_kernels_prepare() != 0) {
+  if (row_kernels_prepare() != 0 || sampler_prepare() != 0) {
     delete c;
     return backend_error("raising the shared-memory limit of the row kernels failed");
   }
@@ -635,6 +638,64 @@ int bitnet_cuda_greedy_argmax(bitnet_cuda_ctx* c, const float* logits, size_t n,
   BN_TRY(c->b[1].ensure(4));
   launch_argmax(c->b[0].as<float>(), (int)n, 1, (int)n, c->b[1].as<uint32_t>(), c->stream);
   BN_CUDA(cudaMemcpyAsync(token, c->b[1].p, 4, cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
+}
+
+// ---- sampling -----------------------------------------------------------------------
+}  // extern "C"
+
+namespace bitnet {
+int validate_sampling(const bitnet_cuda_sampling& cfg, size_t max_new_tokens) {
+  if (!(cfg.temperature > 0.0f))
+    return config_error("temperature must be > 0, got " + std::to_string(cfg.temperature));
+  if (!(cfg.top_p > 0.0f && cfg.top_p <= 1.0f))
+    return config_error("top_p must be in (0, 1], got " + std::to_string(cfg.top_p));
+  if (cfg.repetition_penalty < 1.0f)
+    return config_error("repetition_penalty must be >= 1.0, got " + std::to_string(cfg.repetition_penalty));
+  if (max_new_tokens == 0) return config_error("max_new_tokens must be > 0");
+  return BITNET_OK;
+}
+
+int sample_device(bitnet_cuda_ctx* c, float* d_logits, size_t V, const bitnet_cuda_sampling& cfg,
+                  const uint32_t* d_past, size_t n_past, uint32_t* token, cudaStream_t st) {
+  if (V > 0x7fffffffu || n_past > 0xffffffffu) return shape_error("vocab < 2^31 and history < 2^32", sz(V));
+  BN_TRY(ensure_exp_table(c));
+  void* before = c->samp_counts.p;
+  BN_TRY(c->samp_counts.ensure(V * 4));
+  if (c->samp_counts.p != before) BN_CUDA(cudaMemsetAsync(c->samp_counts.p, 0, c->samp_counts.cap, st));
+  BN_TRY(c->samp_e.ensure(V * 4));
+  BN_TRY(c->samp_misc.ensure(16));
+  BN_CUDA(cudaMemsetAsync(c->samp_misc.p, 0, 16, st));
+  uint32_t* misc = c->samp_misc.as<uint32_t>();
+  launch_sample(d_logits, (uint32_t)V, cfg, d_past, (uint32_t)n_past, c->samp_counts.as<int32_t>(),
+                c->samp_e.as<float>(), misc, reinterpret_cast<int32_t*>(misc + 1), c->exp_table, st);
+  BN_CUDA(cudaGetLastError());
+  uint32_t h[2] = {0, 0};
+  BN_CUDA(cudaMemcpyAsync(h, misc, 8, cudaMemcpyDeviceToHost, st));
+  BN_CUDA(cudaStreamSynchronize(st));
+  if (h[1]) return backend_error("top-p over more than 4096 finite logits is not supported by the device sampler");
+  *token = h[0];
+  return BITNET_OK;
+}
+}  // namespace bitnet
+
+extern "C" {
+
+int bitnet_cuda_sample_next_token(bitnet_cuda_ctx* c, float* logits, size_t vocab, const bitnet_cuda_sampling* cfg,
+                                  const uint32_t* past, size_t n_past, uint32_t* token) {
+  if (!c || !cfg || !token) return shape_error("non-null context, config and token", "null");
+  if (vocab == 0) {
+    *token = 0;
+    return BITNET_OK;
+  }
+  if (!logits || (n_past && !past)) return shape_error("non-null logits and history", "null");
+  Guard g(c);
+  BN_TRY(upload(c->b[0], logits, vocab * 4, c->stream));
+  if (n_past) BN_TRY(upload(c->b[1], past, n_past * 4, c->stream));
+  BN_TRY(sample_device(c, c->b[0].as<float>(), vocab, *cfg, n_past ? c->b[1].as<uint32_t>() : nullptr, n_past, token,
+                       c->stream));
+  // the reference modifies the logits in place (penalty, temperature, masks)
+  BN_CUDA(cudaMemcpyAsync(logits, c->b[0].p, vocab * 4, cudaMemcpyDeviceToHost, c->stream));
   return finish(c);
 }
 

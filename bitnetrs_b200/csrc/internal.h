@@ -55,6 +55,9 @@ struct bitnet_cuda_ctx {
   bool exp_ready = false;
   bitnet::DevBuf exp_keys, exp_vals, exp_hash, exp_en, exp_fj;
   bitnet::ExpTable exp_table;
+  // device sampler scratch: occurrence counts [vocab] (kept at zero between
+  // calls), exp values [vocab], token + status words
+  bitnet::DevBuf samp_counts, samp_e, samp_misc;
 };
 
 struct bitnet_cuda_weight {
@@ -69,4 +72,11 @@ void ctx_retain(bitnet_cuda_ctx* c);
 void ctx_release(bitnet_cuda_ctx* c);
 // Builds ctx->exp_table on first use (caller holds ctx->mu, not capturing).
 int ensure_exp_table(bitnet_cuda_ctx* c);
+// sample_next_token on device logits [vocab] (modified in place) with the
+// device history past[0..n_past); the token comes back to *token (host).
+// Caller holds ctx->mu; synchronises st.
+int sample_device(bitnet_cuda_ctx* c, float* d_logits, size_t vocab, const bitnet_cuda_sampling& cfg,
+                  const uint32_t* d_past, size_t n_past, uint32_t* token, cudaStream_t st);
+// SamplingConfig::validate (crates/bitnet-inference/src/lib.rs:160-178).
+int validate_sampling(const bitnet_cuda_sampling& cfg, size_t max_new_tokens);
 }  // namespace bitnet

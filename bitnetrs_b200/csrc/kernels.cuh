@@ -124,6 +124,14 @@ bool lm_head_mma_supported(int H);
 int lm_head_mma_prepare();  // outside graph capture; 0 on success
 void launch_lm_head_mma(const float* h, int M, int V, int H, const int8_t* W, const float* scales, uint16_t* a3,
                         float* out, int ldo, cudaStream_t st, int32_t* status = nullptr);
+// sample_next_token on one row of logits (sampler.cu): counts is [V] int32
+// kept at zero between calls, escratch [V] floats; status |= 1 when top-p
+// meets more than 4096 finite logits.
+size_t sampler_smem();
+int sampler_prepare();  // outside graph capture; 0 on success
+void launch_sample(float* logits, uint32_t V, const bitnet_cuda_sampling& c, const uint32_t* past, uint32_t n_past,
+                   int32_t* counts, float* escratch, uint32_t* out, int32_t* status, const ExpTable& et,
+                   cudaStream_t st);
 // greedy argmax per row (ties -> last index, NaN compares Equal).
 void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cudaStream_t st);
 

@@ -9,6 +9,8 @@
 // one matmul each.  Every fused step computes the same f32 values as the
 // reference's separate calls.
 #include <algorithm>
+#include <chrono>
+#include <thread>
 #include <tuple>
 #include <cmath>
 #include <cstring>
@@ -61,6 +63,7 @@ struct bitnet_cuda_model {
   float* amax = nullptr;
   int32_t* rowsum = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;
+  uint32_t* hist = nullptr;  // [max_position_embeddings] tokens of the sequence being sampled
   int32_t *tok_pos = nullptr, *tok_seq = nullptr, *last_row = nullptr, *order = nullptr, *status = nullptr;
   DevBuf partial;
   // pinned staging
@@ -86,6 +89,13 @@ struct bitnet_cuda_model {
   ncclResult_t nccl_rc = ncclSuccess;  // first failed collective since the last check
   float *tp_gath = nullptr, *tp_full = nullptr;  // [world][T][C] all-gather, [T][world*C] full rows
   int32_t *tp_acc = nullptr, *tp_rowsum = nullptr;  // [T][H] partial then total accumulators; slice row sums
+  // vocabulary slice of the lm_head: rows [v0, v0 + Vloc) of the table, Vs
+  // columns per rank in `logits` (the last rank's slice may be shorter)
+  int v0 = 0, Vloc = 0, Vs = 0;
+  uint2 *tp_pairs = nullptr, *tp_pairs_all = nullptr;  // [R] this rank's (value, index) argmax, [G][R] all ranks'
+  float *tp_lgath = nullptr, *tp_logits = nullptr;     // [G][R][Vs] all-gathered slices, [R][G*Vs] full rows
+  bool tp_dead = false;  // the communicator was aborted; every later call fails
+  int tp_timeout_ms = 300000;
 
   template <class T>
   int alloc(T** p, size_t n) {
@@ -164,6 +174,8 @@ int check_scale(float s, const char* what) {
   return BITNET_OK;
 }
 
+int model_wait(bitnet_cuda_model* m, cudaStream_t st);
+
 // Ensure sequence `seq` has pages for positions [0, end); update the device table.
 int kv_reserve(bitnet_cuda_kv* kv, uint32_t seq, size_t end, cudaStream_t st) {
   if (end > kv->capacity())
@@ -184,8 +196,7 @@ int kv_reserve(bitnet_cuda_kv* kv, uint32_t seq, size_t end, cudaStream_t st) {
                           (need - first) * sizeof(int32_t), cudaMemcpyHostToDevice, st));
   // the host table entries stay valid until the pages are freed; the copy
   // must finish before they can change
-  BN_CUDA(cudaStreamSynchronize(st));
-  return BITNET_OK;
+  return model_wait(kv->model, st);
 }
 
 // Attention policy: the reference-order kernel serves decode steps and
@@ -244,7 +255,53 @@ void timed(bitnet_cuda_model* m, int cls, cudaStream_t st, F launch) {
 }
 
 void nccl_note(bitnet_cuda_model* m, ncclResult_t r) {
+  // a nonblocking communicator may still be enqueueing the call
+  if (r == ncclInProgress) {
+    const auto t0 = std::chrono::steady_clock::now();
+    do {
+      m->nc->comm_get_async_error(m->comm, &r);
+      if (r != ncclInProgress) break;
+      std::this_thread::yield();
+    } while (std::chrono::steady_clock::now() - t0 < std::chrono::milliseconds(m->tp_timeout_ms));
+  }
   if (r != ncclSuccess && m->nccl_rc == ncclSuccess) m->nccl_rc = r;
+}
+
+// Aborts the communicator of a tensor-parallel model: its pending
+// collectives return, and every later call on the model fails.
+void tp_abort(bitnet_cuda_model* m) {
+  if (m->comm) m->nc->comm_abort(m->comm);
+  m->comm = nullptr;
+  m->tp_dead = true;
+}
+
+// Waits for st.  For a tensor-parallel model the wait also watches the
+// communicator: an asynchronous NCCL error, or no completion within
+// tp_timeout_ms (a peer that left or stopped), aborts the communicator.
+int model_wait(bitnet_cuda_model* m, cudaStream_t st) {
+  if (!m->tp) {
+    BN_CUDA(cudaStreamSynchronize(st));
+    return BITNET_OK;
+  }
+  if (m->tp_dead) return backend_error("the tensor-parallel communicator was aborted after an earlier failure");
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return BITNET_OK;
+    if (e != cudaErrorNotReady) return cuda_error(e, "cudaStreamQuery");
+    ncclResult_t ae = ncclSuccess;
+    m->nc->comm_get_async_error(m->comm, &ae);
+    const bool late = std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(m->tp_timeout_ms);
+    if ((ae != ncclSuccess && ae != ncclInProgress) || late) {
+      std::string why = late ? "no completion within " + std::to_string(m->tp_timeout_ms) + " ms"
+                             : std::string("NCCL error: ") + m->nc->error_string(ae);
+      tp_abort(m);
+      cudaStreamSynchronize(st);  // the aborted collectives have returned
+      cudaGetLastError();
+      return backend_error("tensor-parallel step failed (" + why + "); communicator aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
 }
 
 // Tensor parallelism: all-gather this rank's [T][C] chunk (already in its
@@ -392,15 +449,47 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
   timed(m, kOther, st, [&] {
     launch_rms_norm(m->qrot, H, m->final_norm, H, eps, m->hn, H, n_out, st);
   });
+  // this rank's vocabulary slice (the whole vocabulary without tensor parallelism)
   timed(m, kLmHead, st, [&] {
     if (use_fast_lm_head(m, n_out))
-      launch_lm_head_mma(m->hn, n_out, m->V, H, m->lm_i8, m->lm_scales, m->a3, m->logits, m->V, st, m->status);
+      launch_lm_head_mma(m->hn, n_out, m->Vloc, H, m->lm_i8, m->lm_scales, m->a3, m->logits, m->Vs, st, m->status);
     else
-      launch_lm_head(m->lm_i8, LmW::I8, m->lm_scales, m->hn, H, n_out, m->V, H, m->logits, m->V, st);
+      launch_lm_head(m->lm_i8, LmW::I8, m->lm_scales, m->hn, H, n_out, m->Vloc, H, m->logits, m->Vs, st);
   });
   timed(m, kOther, st, [&] {
-    launch_argmax(m->logits, m->V, n_out, m->V, m->next, st);
+    if (m->tp) {
+      // each rank's best (value, index), all-gathered, the best of those
+      launch_argmax_pairs(m->logits, m->Vs, n_out, m->Vloc, (uint32_t)m->v0, m->tp_pairs, st);
+      nccl_note(m, m->nc->all_gather(m->tp_pairs, m->tp_pairs_all, (size_t)n_out * 2, ncclUint32, m->comm, st));
+      launch_argmax_combine(m->tp_pairs_all, m->tp_world, n_out, m->next, st);
+    } else {
+      launch_argmax(m->logits, m->V, n_out, m->V, m->next, st);
+    }
   });
+}
+
+// Full logits rows [n_out][V] of the last forward: the model's own buffer, or
+// for a tensor-parallel model the all-gather of every rank's slice (a
+// collective: every rank must ask for logits in the same call).  *ld gets
+// the row stride.
+const float* full_logits(bitnet_cuda_model* m, int n_out, size_t* ld, cudaStream_t st) {
+  if (!m->tp) {
+    *ld = (size_t)m->V;
+    return m->logits;
+  }
+  const size_t cnt = (size_t)n_out * m->Vs;
+  nccl_note(m, m->nc->all_gather(m->logits, m->tp_lgath, cnt, ncclFloat32, m->comm, st));
+  launch_tp_unchunk(m->tp_lgath, m->tp_world, n_out, m->Vs, m->tp_logits, st);
+  *ld = (size_t)m->tp_world * m->Vs;
+  return m->tp_logits;
+}
+
+// Copies n_out rows of full logits to dst (row length V).
+int copy_logits(bitnet_cuda_model* m, int n_out, float* dst, cudaMemcpyKind kind, cudaStream_t st) {
+  size_t ld = 0;
+  const float* src = full_logits(m, n_out, &ld, st);
+  BN_CUDA(cudaMemcpy2DAsync(dst, (size_t)m->V * 4, src, ld * 4, (size_t)m->V * 4, (size_t)n_out, kind, st));
+  return BITNET_OK;
 }
 
 // Name of the attention kernel run_forward launches for T tokens (same tests).
@@ -417,7 +506,7 @@ const char* attention_kernel_name(const bitnet_cuda_model* m, const bitnet_cuda_
 int check_status(bitnet_cuda_model* m) {
   int32_t s = 0;
   BN_CUDA(cudaMemcpyAsync(&s, m->status, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
-  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  BN_TRY(model_wait(m, m->ctx->stream));
   if (s) {
     BN_CUDA(cudaMemsetAsync(m->status, 0, 4, m->ctx->stream));
     BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
@@ -507,7 +596,7 @@ int ensure_partial(bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int ma
   size_t bytes = std::max<size_t>(floats, 16) * sizeof(float);
   if (bytes <= m->partial.cap) return BITNET_OK;
   // captured graphs hold the old address
-  BN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  BN_TRY(model_wait(m, m->ctx->stream));
   drop_graphs(m);
   return m->partial.ensure(bytes);
 }
@@ -518,7 +607,9 @@ static void model_release(bitnet_cuda_model* m) {
   if (m->refs.fetch_sub(1) != 1) return;
   bitnet_cuda_ctx* c = m->ctx;
   cudaSetDevice(c->device);
+  if (m->tp && model_wait(m, c->stream) != BITNET_OK) cudaGetLastError();
   cudaStreamSynchronize(c->stream);
+  // graphs that hold NCCL calls go before their communicator
   drop_graphs(m);
   if (m->comm) m->nc->comm_destroy(m->comm);
   for (void* p : m->allocs) cudaFree(p);
@@ -590,10 +681,24 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
     // collective: every rank rendezvouses here before any upload
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof id);
-    ncclResult_t r = nc->comm_init_rank(&m->comm, G, id, rk);
+    // nonblocking init, bounded: a peer that never joins ends it with an error
+    if (const char* t = std::getenv("BITNET_TP_TIMEOUT_MS")) m->tp_timeout_ms = std::max(1, std::atoi(t));
+    ncclConfig_t nc_cfg = NCCL_CONFIG_INITIALIZER;
+    nc_cfg.blocking = 0;
+    ncclResult_t r = nc->comm_init_rank_config(&m->comm, G, id, rk, &nc_cfg);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress && m->comm) {
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(m->tp_timeout_ms)) break;
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+      nc->comm_get_async_error(m->comm, &r);
+    }
     if (r != ncclSuccess) {
+      const std::string why = r == ncclInProgress ? "peers did not join within " + std::to_string(m->tp_timeout_ms) +
+                                                        " ms"
+                                                  : std::string(nc->error_string(r));
+      if (m->comm) nc->comm_abort(m->comm);
       m->comm = nullptr;
-      return fail(backend_error(std::string("ncclCommInitRank: ") + nc->error_string(r)));
+      return fail(backend_error("ncclCommInitRankConfig: " + why));
     }
   }
   DevBuf tmp;
@@ -644,8 +749,14 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
   }
   const size_t V = m->V;
   if ((rc = put(m, &m->embed, w->embed_tokens, V * H))) return fail(rc);
-  if ((rc = put(m, &m->lm_i8, w->lm_head_i8, V * H))) return fail(rc);
-  if ((rc = put(m, &m->lm_scales, w->lm_head_scales, V))) return fail(rc);
+  // lm_head rows: a tensor-parallel rank keeps a slice of 128-row multiples
+  m->Vs = tp ? (int)round_up(ceil_div(V, (size_t)G), 128) : (int)V;
+  m->v0 = tp ? std::min<int>(rk * m->Vs, (int)V) : 0;
+  m->Vloc = tp ? std::min<int>(m->Vs, (int)V - m->v0) : (int)V;
+  if (m->Vloc <= 0) return fail(config_error("vocab_size is too small for the tensor-parallel world"));
+  if (!w->lm_head_i8 || !w->lm_head_scales) return fail(shape_error("non-null lm_head table and scales", "null"));
+  if ((rc = put(m, &m->lm_i8, w->lm_head_i8 + (size_t)m->v0 * H, (size_t)m->Vloc * H))) return fail(rc);
+  if ((rc = put(m, &m->lm_scales, w->lm_head_scales + m->v0, (size_t)m->Vloc))) return fail(rc);
   if ((rc = put(m, &m->final_norm, w->final_norm, H))) return fail(rc);
   {
     size_t smem = paged_attention_exact_smem(m->nh, m->nkv, m->hd, (int)round_up(cfg->max_position_embeddings, kPage));
@@ -693,7 +804,7 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
   if ((rc = m->alloc(&m->attn, T * qd))) return fail(rc);
   if ((rc = m->alloc(&m->gu, T * 2 * F))) return fail(rc);
   if ((rc = m->alloc(&m->hn, R * H))) return fail(rc);
-  if ((rc = m->alloc(&m->logits, R * V))) return fail(rc);
+  if ((rc = m->alloc(&m->logits, R * m->Vs))) return fail(rc);
   if ((rc = m->alloc(&m->a3, R * 3 * H))) return fail(rc);
   if ((rc = m->alloc(&m->xq, T * m->ldq))) return fail(rc);
   if ((rc = m->alloc(&m->amax, T))) return fail(rc);
@@ -704,6 +815,7 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
   if ((rc = m->alloc(&m->tok_seq, T))) return fail(rc);
   if ((rc = m->alloc(&m->last_row, T))) return fail(rc);
   if ((rc = m->alloc(&m->order, T))) return fail(rc);
+  if ((rc = m->alloc(&m->hist, cfg->max_position_embeddings))) return fail(rc);
   if ((rc = m->alloc(&m->status, 16))) return fail(rc);
   if (tp) {
     const size_t wide = (size_t)std::max(m->qd_all, m->F_all);
@@ -711,6 +823,10 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
     if ((rc = m->alloc(&m->tp_full, T * wide))) return fail(rc);
     if ((rc = m->alloc(&m->tp_acc, T * H))) return fail(rc);
     if ((rc = m->alloc(&m->tp_rowsum, T))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_pairs, R))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_pairs_all, R * G))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_lgath, R * G * m->Vs))) return fail(rc);
+    if ((rc = m->alloc(&m->tp_logits, R * G * m->Vs))) return fail(rc);
   }
   cudaError_t e = cudaMallocHost(&m->h_meta, 4 * T * sizeof(int32_t));
   if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
@@ -906,7 +1022,7 @@ static int forward_common(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t n_seq
   BN_TRY(upload_meta(m, T, (int)n_seqs, st));
   run_forward(m, kv, T, (int)n_seqs, max_ctx, st);
   BN_CUDA(cudaGetLastError());
-  if (logits) BN_CUDA(cudaMemcpyAsync(logits, m->logits, n_seqs * m->V * 4, cudaMemcpyDeviceToHost, st));
+  if (logits) BN_TRY(copy_logits(m, (int)n_seqs, logits, cudaMemcpyDeviceToHost, st));
   if (next) BN_CUDA(cudaMemcpyAsync(next, m->next, n_seqs * 4, cudaMemcpyDeviceToHost, st));
   BN_TRY(check_status(m));
   for (size_t i = 0; i < n_seqs; ++i) kv->seq_len[seq_ids[i]] += counts[i];
@@ -967,13 +1083,7 @@ static int decode_graph(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t batch, 
   } else {
     BN_CUDA(cudaMemcpyAsync(m->tokens, src, (size_t)T * 4, cudaMemcpyDeviceToDevice, st));
   }
-  if (m->tp) {
-    // tensor-parallel steps launch eagerly: their NCCL calls are not captured
-    run_forward(m, kv, T, T, max_ctx, st);
-    BN_CUDA(cudaGetLastError());
-    for (size_t i = 0; i < batch; ++i) kv->seq_len[seq_ids[i]] += 1;
-    return BITNET_OK;
-  }
+  if (m->tp_dead) return backend_error("the tensor-parallel communicator was aborted after an earlier failure");
   auto key = std::make_tuple((void*)kv, T, m->timing ? 1 : 0);
   auto it = m->graphs.find(key);
   if (it == m->graphs.end()) {
@@ -1013,7 +1123,7 @@ int bitnet_cuda_decode_step(bitnet_cuda_model* m, bitnet_cuda_kv* kv, size_t bat
   cudaSetDevice(m->ctx->device);
   cudaStream_t st = m->ctx->stream;
   BN_TRY(decode_graph(m, kv, batch, seq_ids, tokens, true, st));
-  if (logits) BN_CUDA(cudaMemcpyAsync(logits, m->logits, batch * m->V * 4, cudaMemcpyDeviceToHost, st));
+  if (logits) BN_TRY(copy_logits(m, (int)batch, logits, cudaMemcpyDeviceToHost, st));
   if (next_tokens) BN_CUDA(cudaMemcpyAsync(next_tokens, m->next, batch * 4, cudaMemcpyDeviceToHost, st));
   return check_status(m);  // synchronises
 }
@@ -1027,7 +1137,7 @@ int bitnet_cuda_decode_step_device(bitnet_cuda_model* m, bitnet_cuda_kv* kv, siz
   cudaStream_t st = stream ? (cudaStream_t)stream : m->ctx->stream;
   BN_TRY(decode_graph(m, kv, batch, seq_ids, d_tokens, false, st));
   BN_CUDA(cudaMemcpyAsync(d_next, m->next, batch * 4, cudaMemcpyDeviceToDevice, st));
-  if (d_logits) BN_CUDA(cudaMemcpyAsync(d_logits, m->logits, batch * m->V * 4, cudaMemcpyDeviceToDevice, st));
+  if (d_logits) BN_TRY(copy_logits(m, (int)batch, d_logits, cudaMemcpyDeviceToDevice, st));
   return BITNET_OK;
 }
 
@@ -1108,6 +1218,53 @@ int bitnet_cuda_generate(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t seq,
     if (next == eos0 || next == eos1) break;
     out_tokens[(*n_out)++] = next;
     BN_TRY(bitnet_cuda_decode_step(m, kv, 1, &seq, &next, nullptr, &next));
+  }
+  return BITNET_OK;
+}
+
+int bitnet_cuda_generate_sampled(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* prompt,
+                                 size_t n_prompt, size_t max_new, const bitnet_cuda_sampling* cfg, uint32_t eos0,
+                                 uint32_t eos1, uint32_t* out_tokens, size_t* n_out) {
+  if (!n_out || !cfg || !m || !kv) return shape_error("non-null model, kv, config and n_out", "null");
+  *n_out = 0;
+  BN_TRY(validate_sampling(*cfg, max_new));  // generate_from_tokens_streaming, lib.rs:706
+  if (n_prompt == 0) return BITNET_OK;
+  if (n_prompt + max_new > m->cfg.max_position_embeddings)
+    return shape_error("prompt + max_new <= max_position_embeddings " + sz(m->cfg.max_position_embeddings),
+                       sz(n_prompt + max_new));
+  BN_TRY(bitnet_cuda_kv_seq_reset(kv, seq));
+  size_t n_hist = n_prompt;
+  uint32_t next = 0;
+  {
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t st = m->ctx->stream;
+    BN_CUDA(cudaMemcpyAsync(m->hist, prompt, n_prompt * 4, cudaMemcpyHostToDevice, st));
+    size_t done = 0;
+    while (done < n_prompt) {
+      uint32_t cnt = (uint32_t)std::min<size_t>(n_prompt - done, (size_t)m->Tmax);
+      BN_TRY(forward_common(m, kv, 1, &seq, &cnt, prompt + done, nullptr, nullptr));
+      done += cnt;
+    }
+    size_t ld = 0;
+    float* lg = const_cast<float*>(full_logits(m, 1, &ld, st));
+    BN_TRY(sample_device(m->ctx, lg, (size_t)m->V, *cfg, m->hist, n_hist, &next, st));
+  }
+  for (size_t step = 0; step < max_new; ++step) {
+    if (next == eos0 || next == eos1) break;
+    out_tokens[(*n_out)++] = next;
+    // the decode step leaves this token's logits in the model's row 0
+    BN_TRY(bitnet_cuda_decode_step(m, kv, 1, &seq, &next, nullptr, nullptr));
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t st = m->ctx->stream;
+    BN_CUDA(cudaMemcpyAsync(m->hist + n_hist, &next, 4, cudaMemcpyHostToDevice, st));
+    ++n_hist;
+    if (step + 1 < max_new) {
+      size_t ld = 0;
+      float* lg = const_cast<float*>(full_logits(m, 1, &ld, st));
+      BN_TRY(sample_device(m->ctx, lg, (size_t)m->V, *cfg, m->hist, n_hist, &next, st));
+    }
   }
   return BITNET_OK;
 }

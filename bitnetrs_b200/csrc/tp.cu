@@ -40,6 +40,9 @@ void load_nccl() {
   }
   g_nccl_ok = resolve(h, "ncclGetUniqueId", &g_nccl.get_unique_id) &&
               resolve(h, "ncclCommInitRank", &g_nccl.comm_init_rank) &&
+              resolve(h, "ncclCommInitRankConfig", &g_nccl.comm_init_rank_config) &&
+              resolve(h, "ncclCommGetAsyncError", &g_nccl.comm_get_async_error) &&
+              resolve(h, "ncclCommAbort", &g_nccl.comm_abort) &&
               resolve(h, "ncclCommDestroy", &g_nccl.comm_destroy) &&
               resolve(h, "ncclAllReduce", &g_nccl.all_reduce) && resolve(h, "ncclAllGather", &g_nccl.all_gather) &&
               resolve(h, "ncclGetErrorString", &g_nccl.error_string);
@@ -109,6 +112,60 @@ void launch_acc_epilogue(const int32_t* acc, int M, int N, float ws, const float
   if (!n) return;
   acc_epilogue_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(acc, M, N, ws, amax, epi == Epi::Residual ? 1 : 0,
                                                                   out, ldo);
+  count_launch();
+}
+
+__device__ __forceinline__ void pair_merge(float& bv, uint32_t& bi, float v, uint32_t i) {
+  if (v > bv || (v == bv && i > bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__global__ void argmax_pairs_kernel(const float* __restrict__ logits, int ld, int V, uint32_t offset,
+                                    uint2* __restrict__ pairs) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* row = logits + (size_t)m * ld;
+  float bv = -INFINITY;
+  uint32_t bi = 0;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) pair_merge(bv, bi, row[v], (uint32_t)v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    pair_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) pair_merge(bv, bi, sv[w], si[w]);
+    pairs[m] = make_uint2(__float_as_uint(bv), bi + offset);
+  }
+}
+
+void launch_argmax_pairs(const float* logits, int ld, int M, int V, uint32_t offset, uint2* pairs, cudaStream_t st) {
+  if (M <= 0) return;
+  argmax_pairs_kernel<<<M, 1024, 0, st>>>(logits, ld, V, offset, pairs);
+  count_launch();
+}
+
+__global__ void argmax_combine_kernel(const uint2* __restrict__ all, int G, int M, uint32_t* __restrict__ out) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float bv = -INFINITY;
+  uint32_t bi = 0;
+  for (int g = 0; g < G; ++g) {
+    const uint2 p = all[(size_t)g * M + m];
+    pair_merge(bv, bi, __uint_as_float(p.x), p.y);
+  }
+  out[m] = bi;
+}
+
+void launch_argmax_combine(const uint2* all, int G, int M, uint32_t* out, cudaStream_t st) {
+  if (M <= 0) return;
+  argmax_combine_kernel<<<(unsigned)ceil_div(M, 256), 256, 0, st>>>(all, G, M, out);
   count_launch();
 }
 

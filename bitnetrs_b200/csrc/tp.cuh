@@ -16,6 +16,9 @@ namespace bitnet {
 struct NcclApi {
   decltype(&ncclGetUniqueId) get_unique_id;
   decltype(&ncclCommInitRank) comm_init_rank;
+  decltype(&ncclCommInitRankConfig) comm_init_rank_config;
+  decltype(&ncclCommGetAsyncError) comm_get_async_error;
+  decltype(&ncclCommAbort) comm_abort;
   decltype(&ncclCommDestroy) comm_destroy;
   decltype(&ncclAllReduce) all_reduce;
   decltype(&ncclAllGather) all_gather;
@@ -38,5 +41,13 @@ void launch_tp_unchunk(const float* src, int G, int T, int C, float* dst, cudaSt
 // stride ldo), the same f32 operations as the fused epilogue.
 void launch_acc_epilogue(const int32_t* acc, int M, int N, float ws, const float* amax, Epi epi, float* out, int ldo,
                          cudaStream_t st);
+
+// Vocabulary-parallel greedy argmax: each row's largest logit of this rank's
+// slice [M][V] (row stride ld) as (value bits, offset + index) in pairs[m];
+// ties to the larger index, as Iterator::max_by (inference/src/lib.rs:263-271).
+void launch_argmax_pairs(const float* logits, int ld, int M, int V, uint32_t offset, uint2* pairs, cudaStream_t st);
+// out[m] = index of the best of the G ranks' pairs all[g][m] (larger value,
+// ties to the larger index).
+void launch_argmax_combine(const uint2* all, int G, int M, uint32_t* out, cudaStream_t st);
 
 }  // namespace bitnet

@@ -290,13 +290,20 @@ class BitNetModel:
         return {c: (float(ms[i]), int(n[i])) for i, c in enumerate(self.KERNEL_CLASSES)}
 
     def generate(self, kv: "KVCache", prompt: Sequence[int], max_new_tokens: int, seq: int = 0,
-                 eos_ids=(EOS_LLAMA3_EOT, EOS_LLAMA3_TEXT)) -> List[int]:
-        """Greedy generation (generate_from_tokens_streaming with top_k = 1)."""
+                 eos_ids=(EOS_LLAMA3_EOT, EOS_LLAMA3_TEXT), sampling=None) -> List[int]:
+        """generate_from_tokens_streaming (crates/bitnet-inference/src/lib.rs:701-777):
+        greedy without `sampling`, else sample_next_token on the device with
+        that SamplingConfig (validated like SamplingConfig::validate)."""
         p = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
         out = np.empty(max(1, max_new_tokens), dtype=np.uint32)
         n = C.c_size_t()
-        check(self._lib.bitnet_cuda_generate(self._h, kv.handle, seq, ptr(p), p.size, max_new_tokens, eos_ids[0],
-                                             eos_ids[1], ptr(out), C.byref(n)))
+        if sampling is None:
+            check(self._lib.bitnet_cuda_generate(self._h, kv.handle, seq, ptr(p), p.size, max_new_tokens,
+                                                 eos_ids[0], eos_ids[1], ptr(out), C.byref(n)))
+        else:
+            check(self._lib.bitnet_cuda_generate_sampled(self._h, kv.handle, seq, ptr(p), p.size, max_new_tokens,
+                                                         C.byref(sampling.to_c()), eos_ids[0], eos_ids[1], ptr(out),
+                                                         C.byref(n)))
         return out[: n.value].tolist()
 
 

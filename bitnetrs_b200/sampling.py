@@ -1,9 +1,9 @@
 """Sampling hyper-parameters of the generate API: SamplingConfig
 (crates/bitnet-inference/src/lib.rs:80-178) with the reference's presets and
-validation rules. Greedy decoding (top_k == 1) is what the device path runs
-today (greedy argmax fused after the lm_head); the full sampler's semantics
-(repetition penalty, temperature, top-k, top-p, the LCG inverse-CDF draw) are
-pinned by the CPU oracle's restatement of sample_next_token.
+validation rules.  The device sampler (bitnet_cuda_sample_next_token,
+CudaBackend.sample_next_token, BitNetModel.generate(sampling=...)) runs the
+reference's sample_next_token on the GPU; greedy decode (top_k == 1) also
+runs as an argmax fused after the lm_head.
 """
 from __future__ import annotations
 
@@ -40,6 +40,11 @@ class SamplingConfig:
         """sample_next_token's greedy shortcut (lib.rs:262-270) applies: the
         argmax of the (penalised, tempered) logits."""
         return self.top_k == 1
+
+    def to_c(self):
+        from ._native import Sampling
+
+        return Sampling(self.temperature, self.top_p, self.top_k, self.repetition_penalty, self.seed)
 
     def with_(self, **kw) -> "SamplingConfig":
         return replace(self, **kw)

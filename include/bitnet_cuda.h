@@ -156,6 +156,28 @@ int bitnet_cuda_ternary_gemv_preq_acc(bitnet_cuda_ctx* ctx, const uint8_t* weigh
  * argmax with ties resolved to the last index, NaN comparing Equal. */
 int bitnet_cuda_greedy_argmax(bitnet_cuda_ctx* ctx, const float* logits, size_t len, uint32_t* token);
 
+/* SamplingConfig (crates/bitnet-inference/src/lib.rs:80-112); max_new_tokens
+ * is the generate call's own argument. */
+typedef struct {
+  float temperature;
+  float top_p;
+  uint32_t top_k;
+  float repetition_penalty;
+  uint64_t seed;
+} bitnet_cuda_sampling;
+
+/* sample_next_token (crates/bitnet-inference/src/lib.rs:236-390) on the GPU:
+ * repetition penalty over past[0..n_past), temperature, the top_k == 1 greedy
+ * shortcut, top-k, top-p, softmax and one LCG step (seed + n_past) for the
+ * inverse-CDF draw, in the reference's arithmetic order (equal
+ * probabilities inside the top-p ordering go in ascending index order; the
+ * reference's sort_unstable leaves that order unspecified).  logits (host,
+ * len vocab) are modified in place as the reference modifies them.  With
+ * top_p < 1, at most 4096 logits may remain finite after top-k, else
+ * BackendError. */
+int bitnet_cuda_sample_next_token(bitnet_cuda_ctx* ctx, float* logits, size_t vocab, const bitnet_cuda_sampling* cfg,
+                                  const uint32_t* past, size_t n_past, uint32_t* token);
+
 /* ===================================================================== */
 /* Device-resident ternary matmul (op sweep, composition)                 */
 /* ===================================================================== */
@@ -368,6 +390,14 @@ int bitnet_cuda_prefill(bitnet_cuda_model* model, bitnet_cuda_kv* kv, size_t n_s
 int bitnet_cuda_generate(bitnet_cuda_model* model, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* prompt,
                          size_t n_prompt, size_t max_new, uint32_t eos0, uint32_t eos1, uint32_t* out_tokens,
                          size_t* n_out);
+
+/* The same loop with sample_next_token on the device: the sampling config
+ * is validated as SamplingConfig::validate (lib.rs:160-178) does, and every
+ * step samples from the last logits with the prompt and the tokens generated
+ * so far as the repetition history (lib.rs:721-733). */
+int bitnet_cuda_generate_sampled(bitnet_cuda_model* model, bitnet_cuda_kv* kv, uint32_t seq, const uint32_t* prompt,
+                                 size_t n_prompt, size_t max_new, const bitnet_cuda_sampling* cfg, uint32_t eos0,
+                                 uint32_t eos1, uint32_t* out_tokens, size_t* n_out);
 
 /* Numerics of the model's forward passes.  The ternary matmul, activation
  * quantisation, norms, RoPE and residual adds are bit-identical to the
