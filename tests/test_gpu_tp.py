@@ -151,14 +151,16 @@ def _tp_leave_rank(rank, world, port, out):
         dist.barrier()
         if rank == 1:
             out.put((1, "left"))
+            out.close()
+            out.join_thread()  # the message is flushed before the process leaves
             os._exit(0)  # leaves without another collective
         t0 = time.monotonic()
         try:
             m.decode_step(kv, [0, 1, 2], nxt)
             out.put((0, "step succeeded without its peer"))
             return
-        except BackendError:
-            pass
+        except BackendError as e:
+            print(f"rank 0: {e} after {time.monotonic() - t0:.1f} s", flush=True)
         waited = time.monotonic() - t0
         try:
             m.decode_step(kv, [0, 1, 2], nxt)
