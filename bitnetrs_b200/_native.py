@@ -126,6 +126,7 @@ _CUDA_SIGS = {
     "bitnet_cuda_model_set_numerics": (i32, [vp, i32]),
     "bitnet_cuda_model_set_kernel_timing": (i32, [vp, i32]),
     "bitnet_cuda_model_kernel_times": (i32, [vp, vp, vp]),
+    "bitnet_cuda_model_set_fused_decode": (i32, [vp, i32]),
     "bitnet_cuda_kernel_launches": (u64, [vp]),
 }
 

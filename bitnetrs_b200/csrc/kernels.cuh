@@ -84,6 +84,14 @@ struct Segments {
   float scale[3] = {0.f, 0.f, 0.f};
 };
 enum class Epi : int { Store = 0, Residual = 1 };
+__device__ __forceinline__ float seg_scale(const Segments& s, int n) {
+  return n < s.end[0] ? s.scale[0] : (n < s.end[1] ? s.scale[1] : s.scale[2]);
+}
+// The reference's dequantisation (bitnet-cpu/src/gemv.rs:297-307): acc as f32 * (ws * act_absmax / 127).
+__device__ __forceinline__ float dequant(int32_t acc, float ws, float amax) {
+  float combined = __fdiv_rn(__fmul_rn(ws, amax), 127.0f);
+  return __fmul_rn((float)acc, combined);
+}
 // out[m][n] = (sum_k W[n,k] x[m][k]) * ((seg_scale*act_absmax[m])/127); Residual: out += that.
 // acc (optional) receives the int32 sums [M][N] (row stride N).
 // `status` (optional) receives kStatusWaitTimeout if the tensor-core kernel
@@ -229,5 +237,47 @@ void launch_kv_fill_random(const KvGeom& kv, const int32_t* page_row, int n, uin
 // Copy positions [0,n) between a host-layout staging buffer [layer][pos][kvh*hd] (f32) and the cache.
 void launch_kv_copy(const KvGeom& kv, const int32_t* page_row, int n, float* k_stage, float* v_stage, bool to_cache,
                     cudaStream_t st);
+
+// ---- whole-layer-stack decode of one token (kernels_decode1.cu) ----
+// Per layer: the device weights of the four projections (qkv, o, gate/up,
+// down), the four norm gains (attn_norm, attn_sub_norm, ffn_norm,
+// ffn_sub_norm) and the seven per-tensor scales.
+struct D1Layer {
+  const uint32_t* w[4];
+  const float* norm[4];
+  float sq, sk, sv, so, sg, su, sd, pad;
+};
+struct D1Params {
+  const D1Layer* layers = nullptr;  // device array [L]
+  int L = 0, H = 0, nh = 0, nkv = 0, F = 0, V = 0;
+  float eps = 0.0f;
+  // shared-memory plan (decode1_plan): matmul CTAs' weight slots, norm row
+  // and int8 row; attention CTAs' ring slots and score rows
+  uint32_t slot_off[4] = {0, 0, 0, 0}, slot_bytes[4] = {0, 0, 0, 0};
+  uint32_t row_off = 0, xq_off = 0, hown_off = 0, sc_off = 0;
+  int hpc = 0;  // query heads per attention CTA (decode1_hpc)
+  int ring_slots = 0, cap = 0;
+  const uint16_t* embed = nullptr;  // [V][H] bf16
+  const uint32_t* token = nullptr;  // the token (device)
+  const int32_t *tok_pos = nullptr, *tok_seq = nullptr, *page_table = nullptr;
+  KvGeom g;
+  const float *rope_cos = nullptr, *rope_sin = nullptr;  // [max_pos][64]
+  ExpTable et;
+  float *h = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr;  // [H], [q+2kv], [q], [2F]
+  int32_t* status = nullptr;
+  uint32_t* sync = nullptr;  // decode1_sync_bytes(), zeroed before every launch
+};
+// Query heads per attention CTA: the smallest divisor of the GQA group (1, 2,
+// 4 or 8) that keeps the attention CTAs to 32; 0 when the group is unsupported.
+int decode1_hpc(int nh, int nkv);
+bool decode1_supported(int nh, int nkv, int H, int F, const KvGeom& g);
+// Fills the shared-memory plan (and hpc) for `sms` CTAs and contexts of up to
+// `cap` positions; the dynamic shared memory of the launch, 0 if over smem_limit.
+size_t decode1_plan(D1Params* P, int sms, int cap, size_t smem_limit);
+size_t decode1_smem_limit(int hpc);  // raises the kernel's limit; outside graph capture; 0 on failure
+bool decode1_fits(int hpc, int grid, size_t smem);  // all `grid` CTAs co-resident
+size_t decode1_sync_bytes();
+// Cooperative launch of `grid` CTAs (grid - nh / hpc matmul CTAs); 0 on success.
+int launch_decode1(const D1Params& P, const CUtensorMap& tmap, int grid, size_t smem, cudaStream_t st);
 
 }  // namespace bitnet

@@ -39,16 +39,6 @@ __device__ __forceinline__ void mma_s8u8(int32_t c[4], const uint32_t a[4], uint
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ float seg_scale(const Segments& s, int n) {
-  return n < s.end[0] ? s.scale[0] : (n < s.end[1] ? s.scale[1] : s.scale[2]);
-}
-
-// The reference's dequantisation: acc as f32 * (ws * act_absmax / 127).
-__device__ __forceinline__ float dequant(int32_t acc, float ws, float amax) {
-  float combined = __fdiv_rn(__fmul_rn(ws, amax), 127.0f);
-  return __fmul_rn((float)acc, combined);
-}
-
 __device__ __forceinline__ void epilogue_store(float* out, int ldo, int m, int n, float v, Epi epi) {
   float* p = out + (size_t)m * ldo + n;
   if (epi == Epi::Residual)

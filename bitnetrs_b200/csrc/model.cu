@@ -96,6 +96,15 @@ struct bitnet_cuda_model {
   float *tp_lgath = nullptr, *tp_logits = nullptr;     // [G][R][Vs] all-gathered slices, [R][G*Vs] full rows
   bool tp_dead = false;  // the communicator was aborted; every later call fails
   int tp_timeout_ms = 300000;
+  // one-token decode steps as one persistent kernel (kernels_decode1.cu)
+  D1Layer* d1_layers = nullptr;  // device copy of the per-layer pointers and scales
+  uint32_t* d1_sync = nullptr;   // the kernel's grid counters
+  size_t d1_limit = 0;           // dynamic shared memory the kernel may use (0: unavailable)
+  int d1_sms = 0;
+  bool d1_enabled = true;        // bitnet_cuda_model_set_fused_decode
+  int d1_cap = 0;                // context capacity of the cached plan (0: none)
+  size_t d1_smem = 0;            // its dynamic shared memory (0: the plan does not fit)
+  D1Params d1_plan;
 
   template <class T>
   int alloc(T** p, size_t n) {
@@ -226,6 +235,59 @@ bool use_x4_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int 
 bool use_exact3_attention(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int max_ctx) {
   return m->exact3_ok && kv->tmap_ok && exact3_supported(kv->g, m->nh) && exact3_smem(max_ctx) <= m->exact3_smem_max;
 }
+// The one-token step runs as decode1_kernel when the model and cache fit it
+// (not tensor-parallel, bf16 cache with its tensor map, head_dim 128, GQA
+// group 1/2/4/8) outside FAST numerics, and d1_prepare planned its shared
+// memory for this context capacity.
+constexpr int kD1CapStep = 256;
+bool decode1_eligible(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T) {
+  return T == 1 && m->d1_enabled && !m->tp && m->numerics != BITNET_NUMERICS_FAST && m->d1_layers && m->d1_limit &&
+         kv->tmap_ok && decode1_supported(m->nh, m->nkv, m->H, m->F, kv->g);
+}
+bool use_decode1(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  return decode1_eligible(m, kv, T) && m->d1_cap == (int)round_up((size_t)max_ctx, kD1CapStep) && m->d1_smem > 0;
+}
+// Plans (and caches) the kernel's shared memory for contexts up to max_ctx;
+// outside graph capture.
+void d1_prepare(bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  if (!decode1_eligible(m, kv, T)) return;
+  const int cap = (int)round_up((size_t)max_ctx, kD1CapStep);
+  if (cap == m->d1_cap) return;
+  D1Params P;
+  P.L = m->L;
+  P.H = m->H;
+  P.nh = m->nh;
+  P.nkv = m->nkv;
+  P.F = m->F;
+  P.V = m->V;
+  P.eps = m->cfg.rms_norm_eps;
+  size_t smem = decode1_plan(&P, m->d1_sms, cap, m->d1_limit);
+  if (smem && !decode1_fits(P.hpc, m->d1_sms, smem)) smem = 0;
+  m->d1_cap = cap;
+  m->d1_smem = smem;
+  m->d1_plan = P;
+}
+void launch_decode1_step(bitnet_cuda_model* m, bitnet_cuda_kv* kv, cudaStream_t st) {
+  D1Params P = m->d1_plan;
+  P.layers = m->d1_layers;
+  P.embed = m->embed;
+  P.token = m->tokens;
+  P.tok_pos = m->tok_pos;
+  P.tok_seq = m->tok_seq;
+  P.page_table = kv->d_table;
+  P.g = kv->g;
+  P.rope_cos = m->rope_cos;
+  P.rope_sin = m->rope_sin;
+  P.et = m->ctx->exp_table;
+  P.h = m->h;
+  P.qkv = m->qkv;
+  P.attn = m->attn;
+  P.gu = m->gu;
+  P.status = m->status;
+  P.sync = m->d1_sync;
+  cudaMemsetAsync(m->d1_sync, 0, decode1_sync_bytes(), st);
+  launch_decode1(P, kv->tmap, m->d1_sms, m->d1_smem, st);
+}
 bool use_fast_lm_head(const bitnet_cuda_model* m, int n_out) {
   if (!m->lm_mma_ok || m->numerics == BITNET_NUMERICS_EXACT) return false;
   return m->numerics == BITNET_NUMERICS_FAST || n_out > kSmallStepTokens;
@@ -235,7 +297,7 @@ bool exact_scores_in_smem(const bitnet_cuda_model* m, int max_ctx) {
 }
 
 // Kernel classes for the per-step timing of device-resident decode graphs.
-enum KClass { kAttn = 0, kMatmul = 1, kNormQuant = 2, kRopeKv = 3, kLmHead = 4, kOther = 5, kClasses = 6 };
+enum KClass { kAttn = 0, kMatmul = 1, kNormQuant = 2, kRopeKv = 3, kLmHead = 4, kOther = 5, kLayers = 6, kClasses = 7 };
 
 // Records an event pair around `launch` when the graph being captured is timed.
 template <class F>
@@ -336,10 +398,13 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
   const int H = m->H, qd = m->qd, kvd = m->kvd, F = m->F;
   const float eps = m->cfg.rms_norm_eps;
   const int nqkv = qd + 2 * kvd;
-  timed(m, kOther, st, [&] {
-    launch_embed(m->embed, m->tokens, T, H, m->h, m->status, m->V, st);
-  });
-  for (int l = 0; l < m->L; ++l) {
+  const bool fused = use_decode1(m, kv, T, max_ctx);
+  if (fused) timed(m, kLayers, st, [&] { launch_decode1_step(m, kv, st); });
+  else
+    timed(m, kOther, st, [&] {
+      launch_embed(m->embed, m->tokens, T, H, m->h, m->status, m->V, st);
+    });
+  for (int l = 0; l < (fused ? 0 : m->L); ++l) {
     const Layer& Lw = m->layers[l];
     // attention block
     timed(m, kNormQuant, st, [&] {
@@ -494,6 +559,7 @@ int copy_logits(bitnet_cuda_model* m, int n_out, float* dst, cudaMemcpyKind kind
 
 // Name of the attention kernel run_forward launches for T tokens (same tests).
 const char* attention_kernel_name(const bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  if (use_decode1(m, kv, T, max_ctx)) return "decode1_kernel";
   if (use_exact_attention(m, T) && use_x4_attention(m, kv, max_ctx)) return "attn_qk_softmax_kernel+attn_pv_kernel";
   if (use_exact_attention(m, T) && use_exact3_attention(m, kv, max_ctx)) return "paged_attention_exact3_kernel";
   if (use_exact_attention(m, T) && use_exact2_attention(m, kv, max_ctx)) return "paged_attention_exact2_kernel";
@@ -585,6 +651,7 @@ void drop_graphs(bitnet_cuda_model* m) {
 }
 
 int ensure_partial(bitnet_cuda_model* m, const bitnet_cuda_kv* kv, int T, int max_ctx) {
+  d1_prepare(m, kv, T, max_ctx);
   size_t floats = use_exact_attention(m, T)
                       ? (use_x4_attention(m, kv, max_ctx) ? attn_x4_scratch_floats(T, m->nkv, max_ctx)
                          : (use_exact3_attention(m, kv, max_ctx) || use_exact2_attention(m, kv, max_ctx) ||
@@ -758,6 +825,39 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
   if ((rc = put(m, &m->lm_i8, w->lm_head_i8 + (size_t)m->v0 * H, (size_t)m->Vloc * H))) return fail(rc);
   if ((rc = put(m, &m->lm_scales, w->lm_head_scales + m->v0, (size_t)m->Vloc))) return fail(rc);
   if ((rc = put(m, &m->final_norm, w->final_norm, H))) return fail(rc);
+  {
+    KvGeom g16;
+    g16.bf16 = 1;
+    g16.hd = 128;
+    if (!tp && m->hd == 128 && decode1_supported(m->nh, m->nkv, H, F, g16)) {
+      std::vector<D1Layer> dl(m->L);
+      for (int l = 0; l < m->L; ++l) {
+        const Layer& a = m->layers[l];
+        D1Layer& b = dl[l];
+        b.w[0] = a.wqkv;
+        b.w[1] = a.wo;
+        b.w[2] = a.wgu;
+        b.w[3] = a.wdown;
+        b.norm[0] = a.attn_norm;
+        b.norm[1] = a.attn_sub_norm;
+        b.norm[2] = a.ffn_norm;
+        b.norm[3] = a.ffn_sub_norm;
+        b.sq = a.sq;
+        b.sk = a.sk;
+        b.sv = a.sv;
+        b.so = a.so;
+        b.sg = a.sg;
+        b.su = a.su;
+        b.sd = a.sd;
+        b.pad = 0.0f;
+      }
+      if ((rc = put(m, &m->d1_layers, dl.data(), dl.size()))) return fail(rc);
+      if ((rc = m->alloc(&m->d1_sync, decode1_sync_bytes() / 4))) return fail(rc);
+      cudaDeviceGetAttribute(&m->d1_sms, cudaDevAttrMultiProcessorCount, ctx->device);
+      const int hpc = decode1_hpc(m->nh, m->nkv);
+      m->d1_limit = m->d1_sms > m->nh / hpc ? decode1_smem_limit(hpc) : 0;
+    }
+  }
   {
     size_t smem = paged_attention_exact_smem(m->nh, m->nkv, m->hd, (int)round_up(cfg->max_position_embeddings, kPage));
     if (smem <= kExactMaxSmem && paged_attention_exact_prepare(smem) == 0) {
@@ -1153,11 +1253,23 @@ int bitnet_cuda_model_set_numerics(bitnet_cuda_model* m, int mode) {
   return BITNET_OK;
 }
 
+int bitnet_cuda_model_set_fused_decode(bitnet_cuda_model* m, int enable) {
+  if (!m) return shape_error("non-null model", "null");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  m->d1_enabled = enable != 0;
+  drop_graphs(m);  // captured graphs embed the previous kernel choice
+  return BITNET_OK;
+}
+
 int bitnet_cuda_model_attention_kernel(bitnet_cuda_model* m, bitnet_cuda_kv* kv, uint32_t tokens, char* name,
                                        size_t name_len) {
   if (!m || !kv || !name || name_len == 0) return shape_error("non-null arguments", "null");
   if (tokens == 0) return shape_error("tokens > 0", "0");
   std::lock_guard<std::mutex> lk(m->ctx->mu);
+  cudaSetDevice(m->ctx->device);
+  d1_prepare(m, kv, (int)tokens, (int)kv->capacity());
   const char* k = attention_kernel_name(m, kv, (int)tokens, (int)kv->capacity());
   std::snprintf(name, name_len, "%s", k);
   return BITNET_OK;

@@ -270,7 +270,13 @@ class BitNetModel:
         """"auto" (reference-order kernels for steps <= 16 tokens), "exact" or "fast"."""
         check(self._lib.bitnet_cuda_model_set_numerics(self._h, self.NUMERICS[mode]))
 
-    KERNEL_CLASSES = ("attention", "ternary_matmul", "norm_quant", "rope_kv_store", "lm_head", "other")
+    KERNEL_CLASSES = ("attention", "ternary_matmul", "norm_quant", "rope_kv_store", "lm_head", "other",
+                      "decode_layers")
+
+    def set_fused_decode(self, enable: bool) -> None:
+        """One-token steps as one persistent kernel over all layers (default on
+        where the model and cache fit it); off selects the per-layer kernels."""
+        check(self._lib.bitnet_cuda_model_set_fused_decode(self._h, 1 if enable else 0))
 
     def set_kernel_timing(self, enable: bool) -> None:
         """Record CUDA events around every kernel of decode graphs captured from now on."""
@@ -284,8 +290,8 @@ class BitNetModel:
 
     def kernel_times(self):
         """{class: (device ms summed over the most recent timed step, launches)}."""
-        ms = np.zeros(6, dtype=np.float32)
-        n = np.zeros(6, dtype=np.int32)
+        ms = np.zeros(len(self.KERNEL_CLASSES), dtype=np.float32)
+        n = np.zeros(len(self.KERNEL_CLASSES), dtype=np.int32)
         check(self._lib.bitnet_cuda_model_kernel_times(self._h, ptr(ms), ptr(n)))
         return {c: (float(ms[i]), int(n[i])) for i, c in enumerate(self.KERNEL_CLASSES)}
 

@@ -416,12 +416,21 @@ int bitnet_cuda_generate_sampled(bitnet_cuda_model* model, bitnet_cuda_kv* kv, u
 #define BITNET_NUMERICS_FAST 2
 int bitnet_cuda_model_set_numerics(bitnet_cuda_model* model, int mode);
 
+/* One-token steps (decode at batch 1, a one-token forward) run every layer
+ * as one persistent kernel when the model and cache fit it: not tensor-
+ * parallel, a bf16 cache, head_dim 128, 1/2/4/8 query heads per kv head, and
+ * the numerics mode is not FAST.  Same operations and order as the per-layer
+ * kernels, so the same results bit for bit.  Enabled by default; 0 selects
+ * the per-layer kernels (for comparison).  No counterpart in the reference. */
+int bitnet_cuda_model_set_fused_decode(bitnet_cuda_model* model, int enable);
+
 /* Per-kernel-class device timing of device-resident decode steps.  When
  * enabled, decode graphs captured afterwards record CUDA events around every
  * kernel launch; bitnet_cuda_model_kernel_times then returns, for the most
  * recent timed step, the summed device time (ms) and the launch count of each
  * class: [0] attention, [1] ternary matmul, [2] RMSNorm+quantise,
- * [3] RoPE + KV store, [4] lm_head, [5] other.  Arrays hold 6 entries. */
+ * [3] RoPE + KV store, [4] lm_head, [5] other, [6] the fused layer stack of
+ * a one-token step (decode1_kernel).  Arrays hold 7 entries. */
 int bitnet_cuda_model_set_kernel_timing(bitnet_cuda_model* model, int enable);
 int bitnet_cuda_model_kernel_times(bitnet_cuda_model* model, float* ms, int32_t* launches);
 
