@@ -4,6 +4,7 @@
 #include "common.cuh"
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 
 namespace bitnet {
 
@@ -238,6 +239,16 @@ void launch_kv_fill_random(const KvGeom& kv, const int32_t* page_row, int n, uin
 void launch_kv_copy(const KvGeom& kv, const int32_t* page_row, int n, float* k_stage, float* v_stage, bool to_cache,
                     cudaStream_t st);
 
+// ---- one-row int8 lm_head + greedy argmax (kernels_lmhead.cu) ----
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();  // the driver's cuTensorMapEncodeTiled (or null)
+bool lm_head_m1_supported(int H, int V);
+size_t lm_head_m1_part_bytes(int V);  // scratch for the per-block argmax states
+int lm_head_m1_prepare(int H);        // outside graph capture; 0 on success
+int lm_head_m1_make_tmap(const int8_t* W, int V, int H, CUtensorMap* map);  // 0 on success
+// logits[v] = dot_f32_i8w(W[v], h) * scales[v] for one row h, and *next = their greedy argmax.
+void launch_lm_head_m1(const CUtensorMap& map, const float* h, const float* scales, int V, int H, float* out,
+                       void* part, uint32_t* next, int32_t* status, cudaStream_t st);
+
 // ---- whole-layer-stack decode of one token (kernels_decode1.cu) ----
 // Per layer: the device weights of the four projections (qkv, o, gate/up,
 // down), the four norm gains (attn_norm, attn_sub_norm, ffn_norm,
@@ -264,6 +275,8 @@ struct D1Params {
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [max_pos][64]
   ExpTable et;
   float *h = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr;  // [H], [q+2kv], [q], [2F]
+  const float* final_norm = nullptr;  // with hn: the final RMSNorm of h is written to hn [H]
+  float* hn = nullptr;
   int32_t* status = nullptr;
   uint32_t* sync = nullptr;  // decode1_sync_bytes(), zeroed before every launch
 };

@@ -440,7 +440,6 @@ __global__ void __launch_bounds__(kX3Threads, 2) paged_attention_exact3_kernel(
 
 namespace bitnet {
 
-namespace {
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -453,7 +452,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   });
   return fn;
 }
-}  // namespace
 
 bool exact3_supported(const KvGeom& kv, int nh) { return kv.bf16 && kv.hd == 128 && nh == 4 * kv.kv_heads; }
 

@@ -268,6 +268,33 @@ __device__ float d1_norm_quant(float4 (&v)[kD1U], const float4 (&wv)[kD1U], cons
   return __fmul_rn(scale, 127.0f);
 }
 
+// 1 / rms of a row in shared memory (rms_inv_exact: the eight FMA chains by
+// lanes 0..7 of warp 0, hsum_f32_avx2, the tail, sqrt(ss / d + eps)), for the
+// final norm.  The caller has synchronised after filling the row.
+__device__ __noinline__ float d1_rms_inv(const float* row, int d, float eps, float* s_bc) {
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    const int chunks = d >> 3;
+    float acc = 0.0f;
+    if (lane < 8)
+      for (int i = 0; i < chunks; ++i) {
+        const float a = row[8 * i + lane];
+        acc = __fmaf_rn(a, a, acc);
+      }
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, acc, j);
+    if (lane == 0) {
+      float ss = hsum8(a);
+      for (int i = chunks * 8; i < d; ++i) ss = __fadd_rn(ss, __fmul_rn(row[i], row[i]));
+      const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps));
+      *s_bc = __fdiv_rn(1.0f, rms);
+    }
+  }
+  __syncthreads();
+  return *s_bc;
+}
+
 // ---------------------------------------------------------------------------
 // The CTA's rows of one projection, from its shared-memory slot: the exact
 // int32 sum of the rowsum identity of gemv_m1_kernel, then the reference's
@@ -729,7 +756,8 @@ __global__ void __launch_bounds__(kD1Threads, 1)
       P.h[r0[1] + i] = hown[i];
     }
   }
-  for (int l = 0; l < L; ++l) {
+  int l = 0;
+  for (; l < L; ++l) {
     const D1Layer& Lw = P.layers[l];
     // ---- attention block ----
     if (l > 0) load_row(v, row, P.h, H);
@@ -781,6 +809,21 @@ __global__ void __launch_bounds__(kD1Threads, 1)
     if (l + 1 < L) {
       norm_gains(wv, P.layers[l + 1].norm[0], H);
       if (!grid_wait(sync, kCtrDown, (uint32_t)((l + 1) * G), status)) break;
+    }
+  }
+  // the final RMSNorm of h (rms_norm_kernel's operations) by the first matmul CTA once every down-projection is in
+  if (l == L && gi == 0 && P.hn && grid_wait(sync, kCtrDown, (uint32_t)(L * G), status)) {
+    norm_gains(wv, P.final_norm, H);
+    load_row(v, row, P.h, H);
+    __syncthreads();
+    const float inv = d1_rms_inv(row, H, P.eps, &s_bc);
+#pragma unroll
+    for (int u = 0; u < kD1U; ++u) {
+      const int j = tid + kD1Threads * u;
+      if (j < (H >> 2))
+        reinterpret_cast<float4*>(P.hn)[j] =
+            make_float4(__fmul_rn(__fmul_rn(v[u].x, inv), wv[u].x), __fmul_rn(__fmul_rn(v[u].y, inv), wv[u].y),
+                        __fmul_rn(__fmul_rn(v[u].z, inv), wv[u].z), __fmul_rn(__fmul_rn(v[u].w, inv), wv[u].w));
     }
   }
   if (tid == 0)  // normally nothing is in flight here; after an abort, issued copies land first (bounded)

@@ -364,4 +364,206 @@ void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cu
   count_launch();
 }
 
+// ---------------------------------------------------------------------------
+// One-row int8 lm_head with the greedy argmax folded in (decode at batch 1).
+// Lane l of warp w owns vocabulary row v = 128 * block + 32 w + l and runs all
+// eight of the reference's FMA chains of that row (dot_f32_i8w_avx2: chain j
+// takes columns 8 i + j, i = 0, 1, ... in order), then hsum_f32_avx2 and the
+// scale, as lm_head_kernel does.  The warp's 32 rows stream through four
+// 4 KiB TMA stages (32 rows x 128 columns, 128-byte swizzle), so each lane
+// reads its row's 16-byte chunks conflict-free.  int8 -> f32 is exact: the
+// byte + 128 is placed in the mantissa of 2^23 and 2^23 + 128 subtracted.
+// Each block leaves the ordered argmax state of its 128 rows; argmax1_kernel
+// combines the blocks in order (same ties and NaN rule as argmax_kernel).
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kL1Warps = 4;
+constexpr int kL1Rows = 32 * kL1Warps;  // rows per block
+constexpr int kL1Stages = 4;
+constexpr int kL1Tile = 32 * 128;       // bytes per stage: 32 rows x 128 columns
+constexpr long long kL1WaitCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t l1_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool l1_wait(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kL1WaitCycles) return false;
+  }
+}
+__device__ __forceinline__ float i8_to_f32(uint32_t u, int k) {  // u = word ^ 0x80808080
+  return __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u | (uint32_t)k)), 8388736.0f);
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kL1Warps * 32) lm_head_m1_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                                   const float* __restrict__ h,
+                                                                   const float* __restrict__ scales, int V, int H,
+                                                                   float* __restrict__ out, ArgState* __restrict__ part,
+                                                                   int32_t* status) {
+  extern __shared__ uint8_t l1_raw[];
+  __shared__ __align__(8) uint64_t bar[kL1Warps][kL1Stages];
+  __shared__ ArgState wst[kL1Warps];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t raw = l1_smem(l1_raw);
+  uint8_t* base = l1_raw + ((1024u - (raw & 1023u)) & 1023u);  // 1024-aligned (128-byte swizzle)
+  float* hs = reinterpret_cast<float*>(base + kL1Warps * kL1Stages * kL1Tile);
+  const int v0 = blockIdx.x * kL1Rows + warp * 32, nst = H / 128;
+  if (lane == 0) {
+    for (int s = 0; s < kL1Stages; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(l1_smem(&bar[warp][s])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  for (int i = tid; i < (H >> 2); i += kL1Warps * 32) reinterpret_cast<float4*>(hs)[i] = reinterpret_cast<const float4*>(h)[i];
+  __syncthreads();
+  const uint32_t tiles = l1_smem(base) + (uint32_t)(warp * kL1Stages * kL1Tile);
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  int issued = 0;  // lane 0: stages issued
+  auto issue = [&](int s) {
+    const uint32_t b = l1_smem(&bar[warp][s % kL1Stages]);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(b), "r"(kL1Tile) : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;\n" ::"r"(tiles + (uint32_t)((s % kL1Stages) * kL1Tile)),
+        "l"((uint64_t)&tmap), "r"(128 * s), "r"(v0), "r"(b), "l"(pol)
+        : "memory");
+    ++issued;
+  };
+  if (lane == 0)
+    for (int s = 0; s < min(kL1Stages, nst); ++s) issue(s);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  bool ok = true;
+  const uint32_t hs_s = l1_smem(hs);
+  for (int s = 0; s < nst; ++s) {
+    ok = __all_sync(0xffffffffu, l1_wait(l1_smem(&bar[warp][s % kL1Stages]), (uint32_t)(s / kL1Stages) & 1u));
+    if (!ok) break;
+    const uint32_t tb = tiles + (uint32_t)((s % kL1Stages) * kL1Tile) + (uint32_t)lane * 128u;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 w;
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                   : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                   : "r"(tb + ((uint32_t)(c ^ (lane & 7)) << 4)));
+      const uint32_t ww[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+      // groups 16 s + 2 c (words 0, 1) and 16 s + 2 c + 1 (words 2, 3)
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        float4 h0, h1;
+        const uint32_t ha = hs_s + (uint32_t)((128 * s + 16 * c + 8 * g) * 4);
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n" : "=f"(h0.x), "=f"(h0.y), "=f"(h0.z), "=f"(h0.w) : "r"(ha));
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n" : "=f"(h1.x), "=f"(h1.y), "=f"(h1.z), "=f"(h1.w) : "r"(ha + 16));
+        const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fmaf_rn(i8_to_f32(ww[2 * g + (j >> 2)], j & 3), hv[j], acc[j]);
+      }
+    }
+    __syncwarp();  // every lane has read the stage before it is refilled
+    if (lane == 0 && s + kL1Stages < nst) issue(s + kL1Stages);
+  }
+  if (!ok) {
+    if (lane == 0) {
+      atomicOr(status, kStatusWaitTimeout);
+      for (int s = 0; s < issued; ++s)  // let issued copies land (bounded) before the CTA exits
+        if (!l1_wait(l1_smem(&bar[warp][s % kL1Stages]), (uint32_t)(s / kL1Stages) & 1u)) break;
+    }
+    return;
+  }
+  const int v = v0 + lane;
+  ArgState st{-1, -1, 0.0f};
+  if (v < V) {
+    const float res = __fmul_rn(hsum8(acc), scales[v]);
+    out[v] = res;
+    if (isnan(res))
+      st.nan_idx = v;
+    else {
+      st.best_idx = v;
+      st.best_val = res;
+    }
+  }
+  for (int o = 1; o < 32; o <<= 1) {
+    ArgState t;
+    t.nan_idx = __shfl_down_sync(0xffffffffu, st.nan_idx, o);
+    t.best_idx = __shfl_down_sync(0xffffffffu, st.best_idx, o);
+    t.best_val = __shfl_down_sync(0xffffffffu, st.best_val, o);
+    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) st = arg_combine(st, t);
+  }
+  if (lane == 0) wst[warp] = st;
+  __syncthreads();
+  if (tid == 0) {
+    ArgState r = wst[0];
+    for (int w = 1; w < kL1Warps; ++w) r = arg_combine(r, wst[w]);
+    part[blockIdx.x] = r;
+  }
+}
+
+// The argmax of the blocks' states, combined in block order.
+__global__ void argmax1_kernel(const ArgState* __restrict__ part, int n, uint32_t* __restrict__ out) {
+  __shared__ ArgState sm[32];
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int b = threadIdx.x * per, e = min(n, b + per);
+  ArgState s{-1, -1, 0.0f};
+  for (int i = b; i < e; ++i) s = arg_combine(s, part[i]);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 1; o < 32; o <<= 1) {
+    ArgState t;
+    t.nan_idx = __shfl_down_sync(0xffffffffu, s.nan_idx, o);
+    t.best_idx = __shfl_down_sync(0xffffffffu, s.best_idx, o);
+    t.best_val = __shfl_down_sync(0xffffffffu, s.best_val, o);
+    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) s = arg_combine(s, t);
+  }
+  if (lane == 0) sm[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ArgState r = sm[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = arg_combine(r, sm[w]);
+    out[0] = r.best_idx >= 0 ? (uint32_t)r.best_idx : (r.nan_idx >= 0 ? (uint32_t)r.nan_idx : 0u);
+  }
+}
+
+bool lm_head_m1_supported(int H, int V) { return H > 0 && H % 128 == 0 && H <= 16384 && V > 0; }
+size_t lm_head_m1_parts(int V) { return (size_t)ceil_div((size_t)V, (size_t)kL1Rows); }
+size_t lm_head_m1_part_bytes(int V) { return lm_head_m1_parts(V) * sizeof(ArgState); }
+static size_t lm_head_m1_smem(int H) { return 1024 + (size_t)kL1Warps * kL1Stages * kL1Tile + (size_t)H * 4; }
+
+int lm_head_m1_prepare(int H) {
+  return cudaFuncSetAttribute(lm_head_m1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lm_head_m1_smem(H)) ==
+                 cudaSuccess
+             ? 0
+             : 1;
+}
+
+// The int8 table [V][H] as a 2-D tensor: x = column (H), y = row (V); a box
+// of 128 x 32 is one stage.
+int lm_head_m1_make_tmap(const int8_t* W, int V, int H, CUtensorMap* map) {
+  if (!lm_head_m1_supported(H, V) || reinterpret_cast<uintptr_t>(W) % 16) return 1;
+  auto enc = tensor_map_encoder();
+  if (!enc) return 1;
+  const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)V};
+  const cuuint64_t strides[1] = {(cuuint64_t)H};
+  const cuuint32_t box[2] = {128, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(W), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1;
+}
+
+void launch_lm_head_m1(const CUtensorMap& map, const float* h, const float* scales, int V, int H, float* out,
+                       void* part, uint32_t* next, int32_t* status, cudaStream_t st) {
+  const unsigned blocks = (unsigned)lm_head_m1_parts(V);
+  lm_head_m1_kernel<<<blocks, kL1Warps * 32, lm_head_m1_smem(H), st>>>(map, h, scales, V, H, out,
+                                                                        reinterpret_cast<ArgState*>(part), status);
+  argmax1_kernel<<<1, 1024, 0, st>>>(reinterpret_cast<const ArgState*>(part), (int)blocks, next);
+  count_launch(2);
+}
+
 }  // namespace bitnet

@@ -105,6 +105,10 @@ struct bitnet_cuda_model {
   int d1_cap = 0;                // context capacity of the cached plan (0: none)
   size_t d1_smem = 0;            // its dynamic shared memory (0: the plan does not fit)
   D1Params d1_plan;
+  // one-row int8 lm_head with the argmax folded in (launch_lm_head_m1)
+  bool lm1_ok = false;
+  CUtensorMap lm1_tmap{};
+  void* lm1_part = nullptr;
 
   template <class T>
   int alloc(T** p, size_t n) {
@@ -285,6 +289,8 @@ void launch_decode1_step(bitnet_cuda_model* m, bitnet_cuda_kv* kv, cudaStream_t 
   P.gu = m->gu;
   P.status = m->status;
   P.sync = m->d1_sync;
+  P.final_norm = m->final_norm;
+  P.hn = m->hn;
   cudaMemsetAsync(m->d1_sync, 0, decode1_sync_bytes(), st);
   launch_decode1(P, kv->tmap, m->d1_sms, m->d1_smem, st);
 }
@@ -507,13 +513,22 @@ void run_forward(bitnet_cuda_model* m, bitnet_cuda_kv* kv, int T, int n_out, int
       });
     }
   }
-  // final norm on the selected rows, lm_head, greedy argmax
-  timed(m, kOther, st, [&] {
-    launch_gather_rows(m->h, H, m->last_row, n_out, m->qrot, st);
-  });
-  timed(m, kOther, st, [&] {
-    launch_rms_norm(m->qrot, H, m->final_norm, H, eps, m->hn, H, n_out, st);
-  });
+  // final norm on the selected rows (the fused layer kernel writes it itself), lm_head, greedy argmax
+  if (!fused) {
+    timed(m, kOther, st, [&] {
+      launch_gather_rows(m->h, H, m->last_row, n_out, m->qrot, st);
+    });
+    timed(m, kOther, st, [&] {
+      launch_rms_norm(m->qrot, H, m->final_norm, H, eps, m->hn, H, n_out, st);
+    });
+  }
+  if (n_out == 1 && m->lm1_ok && !m->tp && !use_fast_lm_head(m, n_out)) {
+    timed(m, kLmHead, st, [&] {
+      launch_lm_head_m1(m->lm1_tmap, m->hn, m->lm_scales, m->Vloc, H, m->logits, m->lm1_part, m->next, m->status,
+                        st);
+    });
+    return;
+  }
   // this rank's vocabulary slice (the whole vocabulary without tensor parallelism)
   timed(m, kLmHead, st, [&] {
     if (use_fast_lm_head(m, n_out))
@@ -825,6 +840,13 @@ int model_create_impl(bitnet_cuda_ctx* ctx, const bitnet_cuda_config* cfg, const
   if ((rc = put(m, &m->lm_i8, w->lm_head_i8 + (size_t)m->v0 * H, (size_t)m->Vloc * H))) return fail(rc);
   if ((rc = put(m, &m->lm_scales, w->lm_head_scales + m->v0, (size_t)m->Vloc))) return fail(rc);
   if ((rc = put(m, &m->final_norm, w->final_norm, H))) return fail(rc);
+  if (!tp && lm_head_m1_supported(H, m->Vloc) && lm_head_m1_prepare(H) == 0 &&
+      lm_head_m1_make_tmap(m->lm_i8, m->Vloc, H, &m->lm1_tmap) == 0) {
+    uint8_t* part = nullptr;
+    if ((rc = m->alloc(&part, lm_head_m1_part_bytes(m->Vloc)))) return fail(rc);
+    m->lm1_part = part;
+    m->lm1_ok = true;
+  }
   {
     KvGeom g16;
     g16.bf16 = 1;
