@@ -65,9 +65,14 @@ def args():
                     help="skip the C2 op sweep (ternary matmul at M in 1..4096 for each 2B projection shape)")
     ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling C4 measurement (N > 1)")
     ap.add_argument("--no-c5", action="store_true", help="skip the C5 tensor-parallel measurement (N > 1)")
-    ap.add_argument("--workload", choices=["c4", "c5"], default="c4",
+    ap.add_argument("--workload", choices=["c4", "c5", "c2"], default="c4",
                     help="c4: data-parallel batch-256 decode of the 2B shape (default); c5: the scaled model "
-                         "tensor-parallel over the job's ranks, batch 64 at context 2048")
+                         "tensor-parallel over the job's ranks, batch 64 at context 2048; c2: only the C2 op "
+                         "sweep (one GPU), e.g. for a profiler capture of one cell")
+    ap.add_argument("--c2-cells", default="",
+                    help="C2 cells to run, e.g. 'gate/up:4096,down:1' (default: every shape and M)")
+    ap.add_argument("--c2-min-bytes", type=float, default=320e6,
+                    help="weight bytes the C2 graph cycles through per cell (default 320 MB, > 2x L2)")
     return ap.parse_args()
 
 
@@ -328,7 +333,7 @@ C2_SHAPES = [("q/o", 2560, 2560), ("k/v", 640, 2560), ("gate/up", 6912, 2560), (
 C2_M = [1, 8, 64, 512, 4096]
 
 
-def c2_sweep(backend, dev, peak_gbs, min_bytes=320e6):
+def c2_sweep(backend, dev, peak_gbs, min_bytes=320e6, cells=None):
     """C2 op sweep: bitnet_cuda_ternary_matmul_device for each 2B projection
     shape at M quantised activation rows, launched back to back in a CUDA
     graph that cycles through enough weight copies (> 2x L2) that the weights
@@ -349,6 +354,8 @@ def c2_sweep(backend, dev, peak_gbs, min_bytes=320e6):
     tops_peak = 2.0 * bf16
     out = {"int8_peak_tops": tops_peak, "hbm_peak_gbs": peak_gbs}
     for name, n, k in C2_SHAPES:
+        if cells is not None and not any(c[0] == name for c in cells):
+            continue
         packed = synth.ternary_codes(SEED, 19, n, k)
         wbytes = n * k / 4
         copies = max(2, int(np.ceil(min_bytes / wbytes)))
@@ -361,6 +368,8 @@ def c2_sweep(backend, dev, peak_gbs, min_bytes=320e6):
         ldq = (k + 63) // 64 * 64
         rows = {}
         for M in C2_M:
+            if cells is not None and (name, M) not in cells:
+                continue
             xb = synth.bf16_normal(SEED, 20 + M, M * k, 1.0)
             d_x = torch.from_numpy(xb.view(np.int16).copy()).to(dev)
             d_xq = torch.zeros(M * ldq, dtype=torch.int8, device=dev)
@@ -852,12 +861,34 @@ def run_c5(a):
     return 0
 
 
+def run_c2(a):
+    """The C2 op sweep alone on one GPU: one JSON line {"c2": ...}."""
+    import torch
+
+    from bitnetrs_b200 import CudaBackend
+
+    cells = None
+    if a.c2_cells:
+        cells = set()
+        for c in a.c2_cells.split(","):
+            name, m = c.rsplit(":", 1)
+            cells.add((name, int(m)))
+    torch.cuda.set_device(0)
+    backend = CudaBackend(0)
+    peak, peak_kind = peaks()
+    c2 = c2_sweep(backend, torch.device("cuda", 0), peak, min_bytes=a.c2_min_bytes, cells=cells)
+    print(json.dumps({"workload": "C2 ternary matmul op sweep", "peak_kind": peak_kind, "c2": c2}), flush=True)
+    return 0
+
+
 def main():
     a = args()
     if a.impl == "reference":
         return run_reference(a)
     if a.workload == "c5":
         return run_c5(a)
+    if a.workload == "c2":
+        return run_c2(a)
     return run_cuda(a)
 
 

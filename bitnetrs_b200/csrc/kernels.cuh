@@ -96,7 +96,7 @@ __device__ __forceinline__ float dequant(int32_t acc, float ws, float amax) {
 // out[m][n] = (sum_k W[n,k] x[m][k]) * ((seg_scale*act_absmax[m])/127); Residual: out += that.
 // acc (optional) receives the int32 sums [M][N] (row stride N).
 // `status` (optional) receives kStatusWaitTimeout if the tensor-core kernel
-// (used for M > 64 when ternary_tc_prepare succeeded) gives up a wait.
+// (used for M > 1 when ternary_tc_prepare succeeded) gives up a wait.
 void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
                            const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo,
                            int32_t* acc, cudaStream_t st, int32_t* status = nullptr);

@@ -335,7 +335,9 @@ void launch_ternary_matmul(const uint32_t* W, int N, int K, const int8_t* xq, in
                            int32_t* acc, cudaStream_t st, int32_t* status) {
   const int kw = (int)words_per_row(K);
   if (M <= 0 || N <= 0) return;
-  if (M > 64 && status && g_tc_ready &&
+  // every multi-row product runs on the tensor cores when they are set up (measured faster than the
+  // mma.sync kernels from M = 8 up, and never slower below)
+  if (M > 1 && status && g_tc_ready &&
       launch_ternary_tc(W, N, K, xq, ldq, act_absmax, row_sum, M, seg, epi, out, ldo, acc, status, st) == 0)
     return;
   if (M == 1) {

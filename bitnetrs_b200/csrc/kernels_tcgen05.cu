@@ -1,6 +1,6 @@
 // kernels_tcgen05.cu — weight-streaming GEMMs on the 5th-generation tensor
 // cores (tcgen05.mma, accumulator in tensor memory) for many activation rows:
-//   * the ternary x int8 matmul (kind::i8) for M > 64 rows (batched decode
+//   * the ternary x int8 matmul (kind::i8) for M > 1 rows (batched decode
 //     and prefill);
 //   * the int8 lm_head for many rows (kind::f16): every int8 weight is exact
 //     in bf16 and the f32 hidden state is the sum of three bf16 terms
