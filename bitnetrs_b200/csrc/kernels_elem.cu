@@ -210,30 +210,32 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   quantize_row_smem(row, d, xq + (size_t)m * ldq, ldq, act_absmax + m, nullptr, row_sum + m, status, red_f, red_i);
 }
 
-// Register-resident variant for rows of at most 8192 values (d % 4 == 0):
-// thread t holds float4 groups t, t + 256, ... of the row. The norm weights
+// Register-resident variant for rows of at most 8192 values with 256 threads
+// or 16384 with 512 (d % 4 == 0): thread t holds float4 groups t, t + NT, ...
+// of the row. The norm weights
 // (no kernel writes them) are loaded before griddepcontrol.wait; lanes 0..7 of
 // warp 0 run the eight FMA chains from a shared copy of the row, their
 // shared-memory loads issued one block of 16 ahead; the rest of the block then
 // normalises, takes the absmax and quantises from registers. Same operations
 // and order as norm_quant_kernel.
-template <bool GATE_UP, int U>
-__global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __restrict__ x, const float* __restrict__ x2,
+template <bool GATE_UP, int U, int NT>
+__global__ void __launch_bounds__(NT) norm_quant_reg_kernel(const float* __restrict__ x, const float* __restrict__ x2,
                                                              int ldx, const float* __restrict__ w, int d, float eps,
                                                              int8_t* __restrict__ xq, int ldq,
                                                              float* __restrict__ act_absmax,
                                                              int32_t* __restrict__ row_sum, int32_t* status) {
   extern __shared__ float4 row4[];  // the row, d / 4 float4
   __shared__ float bc;
-  __shared__ float red_f[8];
-  __shared__ int red_i[8], red_b[8];
+  constexpr int NW = NT / 32;
+  __shared__ float red_f[NW];
+  __shared__ int red_i[NW], red_b[NW];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int m = blockIdx.x, n4 = d >> 2;
   pdl_launch_dependents();
   float4 wv[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    const int j = t + 256 * u;
+    const int j = t + NT * u;
     wv[u] = j < n4 ? reinterpret_cast<const float4*>(w)[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
   pdl_wait();
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
   float4 v[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    const int j = t + 256 * u;
+    const int j = t + NT * u;
     v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (j < n4) {
       float4 a = x4[j];
@@ -300,7 +302,7 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
   int bad = 0;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    if (t + 256 * u < n4) {
+    if (t + NT * u < n4) {
       float4 a = v[u];
       a.x = __fmul_rn(__fmul_rn(a.x, inv), wv[u].x);
       a.y = __fmul_rn(__fmul_rn(a.y, inv), wv[u].y);
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
   }
   __syncthreads();
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < NW; ++k) {
     mx = fmaxf(mx, red_f[k]);
     bad |= red_b[k];
   }
@@ -329,7 +331,7 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
   int sum = 0;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    const int j = t + 256 * u;
+    const int j = t + NT * u;
     if (j < n4) {
       const int8_t c0 = quant_i8(v[u].x, qinv), c1 = quant_i8(v[u].y, qinv), c2 = quant_i8(v[u].z, qinv),
                    c3 = quant_i8(v[u].w, qinv);
@@ -337,7 +339,7 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
       reinterpret_cast<char4*>(q)[j] = make_char4(c0, c1, c2, c3);
     }
   }
-  for (int i = d + t; i < ldq; i += 256) q[i] = 0;  // K padding of the int8 row
+  for (int i = d + t; i < ldq; i += NT) q[i] = 0;  // K padding of the int8 row
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) red_i[warp] = sum;
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(256) norm_quant_reg_kernel(const float* __rest
   if (t == 0) {
     int total = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) total += red_i[k];
+    for (int k = 0; k < NW; ++k) total += red_i[k];
     act_absmax[m] = __fmul_rn(scale, 127.0f);
     row_sum[m] = total;
     if (bad && status) atomicOr(status, 1);
@@ -356,26 +358,35 @@ template <bool GATE_UP>
 static bool launch_norm_quant_reg(const float* x, const float* x2, int ldx, const float* w, int d, float eps,
                                   int8_t* xq, int ldq, float* act_absmax, int32_t* row_sum, int32_t* status, int M,
                                   cudaStream_t st) {
-  const int n4 = d / 4, U = (n4 + 255) / 256;
-  const bool ok = d % 4 == 0 && ldx % 4 == 0 && ldq % 4 == 0 && U >= 1 && U <= 8 &&
+  const int n4 = d / 4, U = (n4 + 255) / 256, U2 = (n4 + 511) / 512;
+  const bool ok = d % 4 == 0 && ldx % 4 == 0 && ldq % 4 == 0 && U >= 1 && U2 <= 8 &&
                   ((uintptr_t)x & 15) == 0 && (!GATE_UP || ((uintptr_t)x2 & 15) == 0) && ((uintptr_t)w & 15) == 0 &&
                   ((uintptr_t)xq & 3) == 0;
   if (!ok) return false;
   const size_t smem = (size_t)d * sizeof(float);
-#define BN_NQ(UU)                                                                                        \
-  case UU:                                                                                               \
-    norm_quant_reg_kernel<GATE_UP, UU><<<M, 256, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq, act_absmax,   \
-                                                           row_sum, status);                             \
+#define BN_NQ(UU, NTT)                                                                                 \
+  case UU:                                                                                             \
+    norm_quant_reg_kernel<GATE_UP, UU, NTT><<<M, NTT, smem, st>>>(x, x2, ldx, w, d, eps, xq, ldq,        \
+                                                                 act_absmax, row_sum, status);         \
     break;
-  switch (U) {
-    BN_NQ(1)
-    BN_NQ(2)
-    BN_NQ(3)
-    BN_NQ(4)
-    BN_NQ(5)
-    BN_NQ(6)
-    BN_NQ(7)
-    BN_NQ(8)
+  if (U <= 8) {
+    switch (U) {
+      BN_NQ(1, 256)
+      BN_NQ(2, 256)
+      BN_NQ(3, 256)
+      BN_NQ(4, 256)
+      BN_NQ(5, 256)
+      BN_NQ(6, 256)
+      BN_NQ(7, 256)
+      BN_NQ(8, 256)
+    }
+  } else {
+    switch (U2) {  // rows of 8193 .. 16384 values: 512 threads
+      BN_NQ(5, 512)
+      BN_NQ(6, 512)
+      BN_NQ(7, 512)
+      BN_NQ(8, 512)
+    }
   }
 #undef BN_NQ
   return true;
@@ -389,6 +400,16 @@ int row_kernels_prepare() {
   bad |= cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
   bad |= cudaFuncSetAttribute(norm_quant_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
   bad |= cudaFuncSetAttribute(norm_quant_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess;
+  // the 512-thread register variants hold rows of up to 16384 floats in shared memory too
+  const int big = 16384 * (int)sizeof(float);
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<true, 5, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<true, 6, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<true, 7, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<true, 8, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<false, 5, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<false, 6, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<false, 7, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
+  bad |= cudaFuncSetAttribute(norm_quant_reg_kernel<false, 8, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess;
   return bad;
 }
 

@@ -369,7 +369,7 @@ void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cu
 // Lane l of warp w owns vocabulary row v = 128 * block + 32 w + l and runs all
 // eight of the reference's FMA chains of that row (dot_f32_i8w_avx2: chain j
 // takes columns 8 i + j, i = 0, 1, ... in order), then hsum_f32_avx2 and the
-// scale, as lm_head_kernel does.  The warp's 32 rows stream through four
+// scale, as lm_head_kernel does.  The warp's 32 rows stream through three
 // 4 KiB TMA stages (32 rows x 128 columns, 128-byte swizzle), so each lane
 // reads its row's 16-byte chunks conflict-free.  int8 -> f32 is exact: the
 // byte + 128 is placed in the mantissa of 2^23 and 2^23 + 128 subtracted.
@@ -379,7 +379,7 @@ void launch_argmax(const float* logits, int ldl, int M, int V, uint32_t* out, cu
 namespace {
 constexpr int kL1Warps = 4;
 constexpr int kL1Rows = 32 * kL1Warps;  // rows per block
-constexpr int kL1Stages = 4;
+constexpr int kL1Stages = 3;  // 3 x 4 warps x 4 KiB + the row: three blocks per SM
 constexpr int kL1Tile = 32 * 128;       // bytes per stage: 32 rows x 128 columns
 constexpr long long kL1WaitCycles = 2000000000LL;
 

@@ -369,3 +369,30 @@ def _raise_invalid_config(backend):
     layers = (N.LayerWeights * 1)()
     wts = N.Weights(None, None, None, None, layers)
     N.check(N.cuda_lib().bitnet_cuda_model_create(backend.handle, C.byref(cfg), C.byref(wts), 8, C.byref(h)))
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_wide_ffn_matches_oracle(cuda_backend, batch):
+    """FFN width 14336 (the scaled model's): the gated sub-norm rows exceed
+    8192 values and take the 512-thread register norm; prefill and decode
+    logits stay bit-identical to the oracle (bf16 cache)."""
+    cfg = ModelConfig(1000, 512, 1, 4, 1, 14336, 256, 500000.0, 1e-5)
+    w = synth.random_model(cfg, seed=44)
+    om = O.OracleModel(w)
+    m = BitNetModel(w, cuda_backend, max_batch_tokens=32)
+    kv = m.new_kv_cache(num_pages=8 * batch, max_seqs=batch, kv_dtype=KV_BF16)
+    prompts = [[(5 * i + 3 * j) % cfg.vocab_size for j in range(4 + i)] for i in range(batch)]
+    nxt, lg = m.prefill(kv, list(range(batch)), prompts, want_logits=True)
+    okvs = [om.kv(64, bf16=True) for _ in range(batch)]
+    ref = [om.forward(okvs[i], prompts[i], 0) for i in range(batch)]
+    for i in range(batch):
+        np.testing.assert_array_equal(lg[i], ref[i])
+    toks = [int(np.argmax(r)) for r in ref]
+    for step in range(2):
+        nxt, lg = m.decode_step(kv, list(range(batch)), toks, want_logits=True)
+        for i in range(batch):
+            r = om.forward(okvs[i], [toks[i]], len(prompts[i]) + step)
+            np.testing.assert_array_equal(lg[i], r, err_msg=f"seq {i} step {step}")
+            toks[i] = int(np.argmax(r))
+    kv.close()
+    m.close()
