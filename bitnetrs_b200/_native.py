@@ -74,6 +74,9 @@ _CUDA_SIGS = {
     "bitnet_cuda_destroy": (None, [vp]),
     "bitnet_cuda_device_name": (C.c_char_p, [vp]),
     "bitnet_cuda_last_error": (C.c_char_p, []),
+    "bitnet_cuda_last_error_expected": (C.c_char_p, []),
+    "bitnet_cuda_last_error_got": (C.c_char_p, []),
+    "bitnet_cuda_kernel_binary_version": (i32, [vp]),
     "bitnet_cuda_version": (C.c_char_p, []),
     "bitnet_cuda_ternary_gemv": (i32, [vp, vp, sz, f32, vp, sz, vp, sz, sz, sz]),
     "bitnet_cuda_ternary_gemv_with_activation_quant": (i32, [vp, vp, sz, f32, vp, sz, vp, sz, sz, sz]),
@@ -189,5 +192,7 @@ def ptr(a):
 def check(code: int) -> None:
     if code != 0:
         from .errors import raise_for
-        msg = cuda_lib().bitnet_cuda_last_error().decode(errors="replace")
-        raise_for(code, msg)
+        lib = cuda_lib()
+        msg = lib.bitnet_cuda_last_error().decode(errors="replace")
+        raise_for(code, msg, lib.bitnet_cuda_last_error_expected().decode(errors="replace"),
+                  lib.bitnet_cuda_last_error_got().decode(errors="replace"))

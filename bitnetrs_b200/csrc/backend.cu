@@ -17,6 +17,8 @@ using namespace bitnet;
 namespace bitnet {
 
 static thread_local std::string g_last_error;
+// the fields of the last InvalidShape { expected, got } (empty after any other error)
+static thread_local std::string g_last_expected, g_last_got;
 
 void set_error(int code, const char* fmt, ...) {
   char buf[1024];
@@ -29,11 +31,16 @@ void set_error(int code, const char* fmt, ...) {
                      : code == BITNET_ERR_INVALID_CONFIG ? "invalid model configuration"
                                                          : "backend error (CUDA)";
   g_last_error = std::string(kind) + ": " + buf;
+  g_last_expected.clear();
+  g_last_got.clear();
 }
 int shape_error(const std::string& expected, const std::string& got) {
   set_error(BITNET_ERR_INVALID_SHAPE, "expected %s, got %s", expected.c_str(), got.c_str());
+  g_last_expected = expected;
+  g_last_got = got;
   return BITNET_ERR_INVALID_SHAPE;
 }
+
 int quant_error(const std::string& msg) {
   set_error(BITNET_ERR_QUANTIZATION, "%s", msg.c_str());
   return BITNET_ERR_QUANTIZATION;
@@ -333,6 +340,16 @@ int device_quantize(bitnet_cuda_ctx* c, const float* x, size_t K, float* scale_o
 extern "C" {
 
 const char* bitnet_cuda_last_error(void) { return g_last_error.c_str(); }
+const char* bitnet_cuda_last_error_expected(void) { return g_last_expected.c_str(); }
+int bitnet_cuda_kernel_binary_version(int32_t* out) {
+  if (!out) return shape_error("non-null out", "null");
+  int v = 0;
+  const int e = kernel_binary_version(&v);
+  if (e) return cuda_error((cudaError_t)e, "cudaFuncGetAttributes");
+  *out = v;
+  return BITNET_OK;
+}
+const char* bitnet_cuda_last_error_got(void) { return g_last_got.c_str(); }
 const char* bitnet_cuda_version(void) { return "bitnetrs-b200 0.1.0 (sm_100a)"; }
 
 int bitnet_cuda_create(uint32_t device_id, bitnet_cuda_ctx** out) {

@@ -109,6 +109,7 @@ int ternary_tc_plan(int N, int K, int M, int* nb, int* stages, int* splits, int*
 int launch_ternary_tc(const uint32_t* W, int N, int K, const int8_t* xq, int ldq, const float* act_absmax,
                       const int32_t* row_sum, int M, const Segments& seg, Epi epi, float* out, int ldo, int32_t* acc,
                       int32_t* status, cudaStream_t st);  // 0 on success
+int kernel_binary_version(int* v);  // binaryVersion of a library kernel; 0 on success
 void set_ternary_tc_ready(bool ready);
 bool ternary_tc_ready();
 // Tensor-core lm_head (kernels_tcgen05.cu): a3 = [M][3H] bf16 terms of h.

@@ -326,6 +326,16 @@ static void run_mma(const uint32_t* W, int N, int kw, const int8_t* xq, int ldq,
   count_launch();
 }
 
+// cudaFuncAttributes::binaryVersion of a kernel of this library on the current
+// device (the SASS architecture the driver loaded, major * 10 + minor).
+int kernel_binary_version(int* v) {
+  cudaFuncAttributes fa{};
+  const cudaError_t e = cudaFuncGetAttributes(&fa, gemv_m1_kernel<1, 2>);
+  if (e != cudaSuccess) return (int)e;
+  *v = fa.binaryVersion;
+  return 0;
+}
+
 static bool g_tc_ready = false;  // ternary_tc_prepare succeeded on every device set up so far
 void set_ternary_tc_ready(bool ready) { g_tc_ready = ready; }
 bool ternary_tc_ready() { return g_tc_ready; }

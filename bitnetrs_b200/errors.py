@@ -21,9 +21,14 @@ class BitNetError(Exception):
 
 
 class InvalidShape(BitNetError):
-    """BitNetError::InvalidShape { expected, got }."""
+    """BitNetError::InvalidShape { expected, got }; both fields are kept."""
 
     code = ERR_INVALID_SHAPE
+
+    def __init__(self, message: str = "", expected: str = "", got: str = ""):
+        super().__init__(message)
+        self.expected = expected
+        self.got = got
 
 
 class QuantizationError(BitNetError):
@@ -47,8 +52,11 @@ class InvalidConfig(BitNetError):
 _BY_CODE = {c.code: c for c in (InvalidShape, QuantizationError, BackendError, InvalidConfig)}
 
 
-def raise_for(code: int, message: str) -> None:
-    """Raise the exception for a non-zero C return code."""
+def raise_for(code: int, message: str, expected: str = "", got: str = "") -> None:
+    """Raise the exception for a non-zero C return code (with the
+    InvalidShape fields when the library reported them)."""
     if code == OK:
         return
+    if code == ERR_INVALID_SHAPE:
+        raise InvalidShape(message, expected, got)
     raise _BY_CODE.get(code, BackendError)(message)

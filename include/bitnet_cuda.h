@@ -65,8 +65,20 @@ const char* bitnet_cuda_device_name(const bitnet_cuda_ctx* ctx);
 /* Message of the last failing call made by this thread ("" if none). */
 const char* bitnet_cuda_last_error(void);
 
+/* The two fields of BitNetError::InvalidShape { expected, got }
+ * (crates/bitnet-core/src/error.rs:17-18) when the last failing call of this
+ * thread returned BITNET_ERR_INVALID_SHAPE; "" after any other error.  The
+ * message above is their Display form ("expected {expected}, got {got}"). */
+const char* bitnet_cuda_last_error_expected(void);
+const char* bitnet_cuda_last_error_got(void);
+
 /* Library version string. */
 const char* bitnet_cuda_version(void);
+
+/* cudaFuncAttributes::binaryVersion of the library's kernels on the current
+ * device: the SASS architecture the driver loaded them for (major * 10 +
+ * minor; 100 for the sm_100a build).  No counterpart in the reference. */
+int bitnet_cuda_kernel_binary_version(int32_t* out);
 
 /* ===================================================================== */
 /* Backend trait methods (host slices)                                    */

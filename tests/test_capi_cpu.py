@@ -37,14 +37,32 @@ def test_python_bindings_cover_header():
     assert sorted(N.exported_cuda_symbols()) == declared_functions()
 
 
-def test_library_is_sm100a_only():
+def test_build_recipe_targets_sm100a_only():
+    """Every object is compiled for sm_100a alone (no PTX, no other SASS);
+    the GPU test test_gpu_ops.py::test_kernels_loaded_for_sm100 checks the
+    binary version the driver actually loads."""
+    from bitnetrs_b200 import build
+
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert build.NVCC_FLAGS[: len(build.ARCH)] == build.ARCH
+    assert not any("compute_" in f and f not in build.ARCH for f in build.NVCC_FLAGS)
+
+
+def test_invalid_shape_fields_without_gpu():
+    """BitNetError::InvalidShape keeps `expected` and `got` apart across the C
+    ABI; any other error clears them."""
+    from bitnetrs_b200 import InvalidShape
     from bitnetrs_b200 import _native as N
 
-    out = subprocess.run(["cuobjdump", "--list-elf", str(N.CUDA_LIB_PATH)], capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    arches = set(re.findall(r"sm_(\d+a?)", out.stdout))
-    assert arches == {"100a"}, arches
+    lib = N.cuda_lib()
+    with pytest.raises(InvalidShape) as ei:
+        N.check(lib.bitnet_cuda_model_check(None))
+    assert ei.value.expected == "non-null model" and ei.value.got == "null"
+    assert str(ei.value) == "invalid tensor shape: expected non-null model, got null"
+    assert lib.bitnet_cuda_last_error_expected() == b"non-null model"
+    h = C.c_void_p()
+    if lib.bitnet_cuda_create(10**6, C.byref(h)) != 0:  # no such device: a backend error
+        assert lib.bitnet_cuda_last_error_expected() == b"" and lib.bitnet_cuda_last_error_got() == b""
 
 
 def test_version_and_error_without_gpu():

@@ -316,3 +316,15 @@ def test_argmax_random(cuda_backend, n):
     if n > 10:
         x[n // 3] = x[2 * n // 3] = x.max() + 1  # tie -> later index
     assert cuda_backend.greedy_argmax(x) == L.orc_greedy_argmax(p(x), n)
+
+
+def test_kernels_loaded_for_sm100(cuda_backend):
+    """The driver loads the library's kernels as sm_100 SASS (the build embeds
+    sm_100a only, so there is no PTX to fall back to)."""
+    import ctypes as C
+
+    from bitnetrs_b200 import _native as N
+
+    v = C.c_int32(0)
+    N.check(N.cuda_lib().bitnet_cuda_kernel_binary_version(C.byref(v)))
+    assert v.value == 100, v.value
