@@ -93,6 +93,29 @@ __device__ __forceinline__ int warp_sum_i(int v) {
   return v;
 }
 
+// Code dot products without shifts.  Masking a packed word in place leaves
+// the codes of elements 4i..4i+3 in bits 2i..2i+1 of each byte, i.e. scaled
+// by 4^i; dp4a with unsigned bytes (the scaled code is at most 2 << 6 = 128)
+// and signed int8 activations accumulates 4^i * sum(c * x) exactly into
+// acc[i].  codes_sum() undoes the scale: every term of acc[i] is a multiple of
+// 4^i, so the arithmetic shift is exact (|acc[3]| < 2^31 for rows of up to
+// 2^21 codes).  Two logic ops fewer per word than shift-and-mask.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// acc[i] += 4^i * sum_j code(element 4i + j of w) * byte j of x_i
+__device__ __forceinline__ void dp4a_word_scaled(uint32_t w, const uint4& x, int (&acc)[4]) {
+  acc[0] = dp4a_us(w & 0x03030303u, (int)x.x, acc[0]);
+  acc[1] = dp4a_us(w & 0x0C0C0C0Cu, (int)x.y, acc[1]);
+  acc[2] = dp4a_us(w & 0x30303030u, (int)x.z, acc[2]);
+  acc[3] = dp4a_us(w & 0xC0C0C0C0u, (int)x.w, acc[3]);
+}
+__device__ __forceinline__ int codes_sum(const int (&acc)[4]) {
+  return acc[0] + (acc[1] >> 2) + (acc[2] >> 4) + (acc[3] >> 6);
+}
+
 // Block-wide reductions for blockDim.x a multiple of 32 (<= 1024).
 template <class T, class Op>
 __device__ __forceinline__ T block_reduce(T v, Op op, T* smem32) {

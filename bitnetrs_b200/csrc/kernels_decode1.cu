@@ -55,6 +55,29 @@ __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+// Slot and phase parity of one item of an attention CTA's ring of S slots
+// (item A sits in slot A % S and completes phase (A / S) & 1 of its
+// barrier), advanced without integer division.
+struct RingPos {
+  int slot;
+  uint32_t par;
+};
+__device__ __forceinline__ RingPos ring_add(RingPos p, int k, int S) {  // 0 <= k <= S
+  p.slot += k;
+  if (p.slot >= S) {
+    p.slot -= S;
+    p.par ^= 1u;
+  }
+  return p;
+}
+__device__ __forceinline__ RingPos ring_advance(RingPos p, int k, int S) {  // any k >= 0
+  while (k > S) {
+    p = ring_add(p, S, S);
+    k -= S;
+  }
+  return ring_add(p, k, S);
+}
 __device__ __forceinline__ uint16_t lds16(uint32_t a) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(a));
@@ -188,20 +211,23 @@ __device__ float d1_norm_quant(float4 (&v)[kD1U], const float4 (&wv)[kD1U], cons
     if (lane < 8) {
       // element 8 i + lane of the row at byte 32 i + 4 lane
       const uint32_t rs = smem_u32(row) + 4u * (uint32_t)lane;
-      const int full = chunks & ~15;
-      float cur[16];
+      // two 16-element register blocks in turn: one block's loads are in
+      // flight while the other's FMAs run, with no register copies in the loop
+      const int full = chunks & ~31;
+      float ba[16], bb[16];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) cur[k] = full ? lds32f(rs + 32u * (uint32_t)k) : 0.0f;
+      for (int k = 0; k < 16; ++k) ba[k] = full ? lds32f(rs + 32u * (uint32_t)k) : 0.0f;
       int i = 0;
-      for (; i < full; i += 16) {
-        float nxt[16];
-        const int ni = i + 16 < full ? i + 16 : i;
+      for (; i < full; i += 32) {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) nxt[k] = lds32f(rs + 32u * (uint32_t)(ni + k));
+        for (int k = 0; k < 16; ++k) bb[k] = lds32f(rs + 32u * (uint32_t)(i + 16 + k));
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(cur[k], cur[k], acc);
+        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(ba[k], ba[k], acc);
+        const int ni = i + 32 < full ? i + 32 : i;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
+        for (int k = 0; k < 16; ++k) ba[k] = lds32f(rs + 32u * (uint32_t)(ni + k));
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(bb[k], bb[k], acc);
       }
       for (; i < chunks; ++i) {
         const float a = lds32f(rs + 32u * (uint32_t)i);
@@ -320,13 +346,6 @@ __device__ __forceinline__ D1Epi d1_epi(float s0, float s1, float s2, int end0, 
   return e;
 }
 
-__device__ __forceinline__ int dp4a_word(uint32_t w, const uint4& x, int acc) {
-  acc = __dp4a((int)(w & 0x03030303u), (int)x.x, acc);
-  acc = __dp4a((int)((w >> 2) & 0x03030303u), (int)x.y, acc);
-  acc = __dp4a((int)((w >> 4) & 0x03030303u), (int)x.z, acc);
-  return __dp4a((int)((w >> 6) & 0x03030303u), (int)x.w, acc);
-}
-
 __device__ __forceinline__ void d1_put(int r, int s, int xsum, const D1Epi& ep, int n0, float* out, float* hown) {
   const int n = n0 + r;
   const float comb = n < ep.end0 ? ep.comb[0] : (n < ep.end1 ? ep.comb[1] : ep.comb[2]);
@@ -362,24 +381,24 @@ __device__ __forceinline__ void d1_gemv(uint32_t ws, int nrows, int kw4, const u
   for (int r = warp; r < nrows; r += 2 * kD1Warps) {
     const int r2 = r + kD1Warps;
     const bool two = r2 < nrows;
-    int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+    int a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
       const int c = lane + 32 * j;
       if (c < kw4) {
         const uint4 w = lds128(ws + (uint32_t)(r * kw4 + c) * 16u);
         const uint4 w2 = two ? lds128(ws + (uint32_t)(r2 * kw4 + c) * 16u) : make_uint4(0, 0, 0, 0);
-        a0 = dp4a_word(w.x, xr[j][0], a0);
-        a1 = dp4a_word(w.y, xr[j][1], a1);
-        b0 = dp4a_word(w2.x, xr[j][0], b0);
-        b1 = dp4a_word(w2.y, xr[j][1], b1);
-        a0 = dp4a_word(w.z, xr[j][2], a0);
-        a1 = dp4a_word(w.w, xr[j][3], a1);
-        b0 = dp4a_word(w2.z, xr[j][2], b0);
-        b1 = dp4a_word(w2.w, xr[j][3], b1);
+        dp4a_word_scaled(w.x, xr[j][0], a);
+        dp4a_word_scaled(w2.x, xr[j][0], b);
+        dp4a_word_scaled(w.y, xr[j][1], a);
+        dp4a_word_scaled(w2.y, xr[j][1], b);
+        dp4a_word_scaled(w.z, xr[j][2], a);
+        dp4a_word_scaled(w2.z, xr[j][2], b);
+        dp4a_word_scaled(w.w, xr[j][3], a);
+        dp4a_word_scaled(w2.w, xr[j][3], b);
       }
     }
-    const int s = warp_sum_i(a0 + a1), s2 = warp_sum_i(b0 + b1);
+    const int s = warp_sum_i(codes_sum(a)), s2 = warp_sum_i(codes_sum(b));
     if (lane == 0) {
       d1_put(r, s, xsum, ep, n0, out, hown);
       if (two) d1_put(r2, s2, xsum, ep, n0, out, hown);
@@ -395,6 +414,12 @@ __device__ __forceinline__ void d1_gemv_any(uint32_t ws, int nrows, int kw4, con
     d1_gemv<2>(ws, nrows, kw4, xs, ep, n0, out, hown);
   else
     d1_gemv<4>(ws, nrows, kw4, xs, ep, n0, out, hown);
+}
+
+// The 16 V values of one page at the lane's dimension (row offsets voff).
+__device__ __forceinline__ void d1_load_v(float (&vv)[kPage], uint32_t vb, const uint32_t (&voff)[4]) {
+#pragma unroll
+  for (int rr = 0; rr < kPage; ++rr) vv[rr] = bf16_bits_to_f32(lds16(vb + (uint32_t)rr * 256u + voff[rr & 3]));
 }
 
 // Rotates (lo, hi) = (x[p], x[p + 64]) of one head (rope.rs:414-431, half split).
@@ -470,10 +495,21 @@ __global__ void __launch_bounds__(kD1Threads, 1)
       }
     };
     auto item_wait = [&](int A) { return mbar_wait(smem_u32(&bar[A % S]), (uint32_t)(A / S) & 1u, nullptr); };
+    auto ring_wait = [&](RingPos a) { return mbar_wait(smem_u32(&bar[a.slot]), a.par, nullptr); };
+    RingPos lpos = {0, 0u};  // ring position of the first item of layer l
     int consumed = 0;  // items every thread has finished reading
     issue_upto(S);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
     const uint32_t qs_s = smem_u32(qs);
+    // PV: lane (warp < 4) owns dimension 32 warp + lane; byte offset of its
+    // value in row rr of a V tile is rr * 256 + voff[rr & 3] (128-byte swizzle)
+    uint32_t voff[4];
+    {
+      const int dd = 32 * warp + lane, half = (dd >> 6) & 1;
+      const uint32_t cw = (uint32_t)((dd & 63) >> 3), bo = (uint32_t)(dd & 7) * 2;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) voff[k] = (uint32_t)half * 128u + ((cw ^ (uint32_t)(2 * k + half)) << 4) + bo;
+    }
     bool alive = true;
     for (int l = 0; l < L && alive; ++l) {
       const int base = l * 2 * np;
@@ -520,14 +556,16 @@ __global__ void __launch_bounds__(kD1Threads, 1)
       {
         const int r = lane & 15, hp = lane >> 4;
         const uint32_t xo0 = (uint32_t)((2 * r) & 7) << 4, xo1 = (uint32_t)((2 * r + 1) & 7) << 4;
+        RingPos rp = lpos;  // item base + p0
         for (int p0 = 0; p0 < np; p0 += RP) {
           const int pend = min(np, p0 + RP), pw = p0 + 2 * warp;
           int ok = 1;
           if (pw < pend) {
-            ok = item_wait(base + pw) && (pw + 1 >= pend || item_wait(base + pw + 1));
+            const RingPos ia = ring_add(rp, 2 * warp, S), ib = ring_add(ia, 1, S);
+            ok = ring_wait(ia) && (pw + 1 >= pend || ring_wait(ib));
             const int pa = pw + hp;
             if (ok && pa < pend) {
-              const uint32_t ba = sm_s + (uint32_t)((base + pa) % S) * kD1Page + (uint32_t)(2 * r) * 128;
+              const uint32_t ba = sm_s + (uint32_t)(hp ? ib.slot : ia.slot) * kD1Page + (uint32_t)(2 * r) * 128;
               const uint32_t c0 = ba | xo0, c1 = (ba + 128) | xo1;
               float acc[HPC][8];
 #pragma unroll
@@ -566,24 +604,28 @@ __global__ void __launch_bounds__(kD1Threads, 1)
           }
           consumed = base + pend;
           issue_upto(min(consumed + S, base + 2 * np));  // this layer's pages first
+          rp = ring_add(rp, pend - p0, S);
         }
       }
       if (!alive) break;
       // ---- the new position's scores, from kn ----
-      if (warp == 0 && lane < HPC) {
-        float acc[8];
+      // (lane j of each group of eight runs FMA chain j of one head; the
+      // group's first lane combines the chains in hsum_f32_avx2 order)
+      if (warp * 32 < 8 * HPC) {
+        const int j = lane & 7, h = min(tid >> 3, HPC - 1);
+        float acc = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-#pragma unroll 4
-        for (int c = 0; c < 16; ++c)
+        for (int c = 0; c < 16; ++c) acc = __fmaf_rn(qs[h * 128 + 8 * c + j], bf16_bits_to_f32(kn[8 * c + j]), acc);
+        float a[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            acc[j] = __fmaf_rn(qs[lane * 128 + 8 * c + j], bf16_bits_to_f32(kn[8 * c + j]), acc[j]);
-        const float sv = __fmul_rn(hsum8(acc), scale);
-        sc[pos * HPC + lane] = sv;
+        for (int jj = 0; jj < 8; ++jj) a[jj] = __shfl_sync(0xffffffffu, acc, (lane & ~7) + jj);
+        if (j == 0 && tid < 8 * HPC) {
+          const float sv = __fmul_rn(hsum8(a), scale);
+          sc[pos * HPC + h] = sv;
 #pragma unroll
-        for (int h = 0; h < HPC; ++h)
-          if (h == lane) mx[h] = fmaxf(mx[h], sv);
+          for (int hh = 0; hh < HPC; ++hh)
+            if (hh == h) mx[hh] = fmaxf(mx[hh], sv);
+        }
       }
 #pragma unroll
       for (int h = 0; h < HPC; ++h) {
@@ -604,61 +646,78 @@ __global__ void __launch_bounds__(kD1Threads, 1)
       if (tid < HPC) {
         const float* e = sc + tid;
         const int full = ctx & ~15;
-        float sum = 0.0f, a[16];
+        float sum = 0.0f;
+        int i = 0;
+        for (; i < full; i += 16) {
+          float a[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) a[k] = full ? e[HPC * k] : 0.0f;
-        for (int i = 0; i < full; i += 16) {
-          float b[16];
-          const int nx = i + 16 < full ? i + 16 : i;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) b[k] = e[HPC * (nx + k)];
+          for (int k = 0; k < 16; ++k) a[k] = e[HPC * (i + k)];
 #pragma unroll
           for (int k = 0; k < 16; ++k) sum = __fadd_rn(sum, a[k]);
-#pragma unroll
-          for (int k = 0; k < 16; ++k) a[k] = b[k];
         }
-        for (int i = full; i < ctx; ++i) sum = __fadd_rn(sum, e[HPC * i]);
+        if (i < ctx) {
+          float a[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) a[k] = i + k < ctx ? e[HPC * (i + k)] : 0.0f;
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            if (i + k < ctx) sum = __fadd_rn(sum, a[k]);
+        }
         s_inv[tid] = __fdiv_rn(1.0f, sum);
       }
       __syncthreads();
       for (int i = tid; i < ctx * HPC; i += kD1Threads) sc[i] = __fmul_rn(sc[i], s_inv[i & (HPC - 1)]);
       __syncthreads();
       // ---- out[h][d] = fma(p_t, V[t][d], out[h][d]) over t (axpy_f32): warps 0..3, lane = dim ----
+      //      (the next page's V values are loaded while this page's FMAs run)
       float o[HPC];
 #pragma unroll
       for (int h = 0; h < HPC; ++h) o[h] = 0.0f;
-      const int d = 32 * warp + lane, half = (d >> 6) & 1;
-      const uint32_t cw = (uint32_t)((d & 63) >> 3), bo = (uint32_t)(d & 7) * 2;
+      const int d = 32 * warp + lane;
+      RingPos vp = ring_advance(lpos, np, S);  // item base + np + P0
       for (int P0 = 0; P0 < np; P0 += RP) {
         const int pend = min(np, P0 + RP);
         int ok = 1;
         if (warp < 4) {
+          RingPos cur = vp;
+          float vv[kPage];
+          ok = ring_wait(cur);
+          if (ok) d1_load_v(vv, sm_s + (uint32_t)cur.slot * kD1Page, voff);
           for (int pg = P0; pg < pend && ok; ++pg) {
-            const int A = base + np + pg;
-            ok = item_wait(A);
-            if (!ok) break;
-            const uint32_t vb = sm_s + (uint32_t)(A % S) * kD1Page;
-            const float* pp = sc + pg * kPage * HPC;
             const int rows = min(kPage, pos - pg * kPage);  // positions < pos of this page
-            if (rows == kPage) {
-              float vv[kPage];
+            // the page's p rows [16][HPC] into registers first (HPC <= 2: 4 HPC
+            // 16-byte loads; rows past pos read scores of this page, unused)
+            constexpr int kPr = HPC <= 2 ? kPage * HPC : 1;
+            float pr[kPr];
+            const float* pp = sc + pg * kPage * HPC;
+            if constexpr (HPC <= 2) {
+              const uint32_t pa = smem_u32(pp);
 #pragma unroll
-              for (int rr = 0; rr < kPage; ++rr) {
-                const uint32_t u = (uint32_t)(2 * rr + half);
-                vv[rr] = bf16_bits_to_f32(lds16(vb + u * 128u + ((cw ^ (u & 7u)) << 4) + bo));
-              }
-#pragma unroll
-              for (int rr = 0; rr < kPage; ++rr)
-#pragma unroll
-                for (int h = 0; h < HPC; ++h) o[h] = __fmaf_rn(pp[rr * HPC + h], vv[rr], o[h]);
-            } else {
-              for (int rr = 0; rr < rows; ++rr) {
-                const uint32_t u = (uint32_t)(2 * rr + half);
-                const float vf = bf16_bits_to_f32(lds16(vb + u * 128u + ((cw ^ (u & 7u)) << 4) + bo));
-#pragma unroll
-                for (int h = 0; h < HPC; ++h) o[h] = __fmaf_rn(pp[rr * HPC + h], vf, o[h]);
+              for (int q = 0; q < kPr / 4; ++q) {
+                const float4 t4 = lds128f(pa + 16u * (uint32_t)q);
+                pr[4 * q] = t4.x;
+                pr[4 * q + 1] = t4.y;
+                pr[4 * q + 2] = t4.z;
+                pr[4 * q + 3] = t4.w;
               }
             }
+            const RingPos nx = ring_add(cur, 1, S);
+            float vnx[kPage];
+            if (pg + 1 < pend) {
+              ok = ring_wait(nx);
+              if (ok) d1_load_v(vnx, sm_s + (uint32_t)nx.slot * kD1Page, voff);
+            }
+#pragma unroll
+            for (int rr = 0; rr < kPage; ++rr)
+              if (rr < rows)
+#pragma unroll
+                for (int h = 0; h < HPC; ++h) {
+                  const float pv = HPC <= 2 ? pr[(rr * HPC + h) % kPr] : pp[rr * HPC + h];
+                  o[h] = __fmaf_rn(pv, vv[rr], o[h]);
+                }
+#pragma unroll
+            for (int rr = 0; rr < kPage; ++rr) vv[rr] = vnx[rr];
+            cur = nx;
           }
         }
         if (!__syncthreads_and(ok)) {
@@ -668,6 +727,7 @@ __global__ void __launch_bounds__(kD1Threads, 1)
         }
         consumed = base + np + pend;
         issue_upto(min(consumed + S, base + 2 * np));
+        vp = ring_add(vp, pend - P0, S);
       }
       if (!alive) break;
       if (warp < 4) {
@@ -680,6 +740,7 @@ __global__ void __launch_bounds__(kD1Threads, 1)
       }
       grid_arrive(sync, kCtrAttn);
       issue_upto(consumed + S);  // the ring runs on into the next layer's pages while the grid works
+      lpos = ring_advance(lpos, 2 * np, S);
     }
     if (!alive && tid == 0) {
       // let the copies this CTA issued land before it exits (bounded)
@@ -759,11 +820,14 @@ __global__ void __launch_bounds__(kD1Threads, 1)
   int l = 0;
   for (; l < L; ++l) {
     const D1Layer& Lw = P.layers[l];
+    // the layer's scales, loaded ahead of the norms that precede their use
+    const float l_sq = __ldg(&Lw.sq), l_sk = __ldg(&Lw.sk), l_sv = __ldg(&Lw.sv), l_so = __ldg(&Lw.so),
+                l_sg = __ldg(&Lw.sg), l_su = __ldg(&Lw.su), l_sd = __ldg(&Lw.sd);
     // ---- attention block ----
     if (l > 0) load_row(v, row, P.h, H);
     float am = d1_norm_quant(v, wv, row, H, P.eps, xq, kw4[0] * 64, &s_bc, red_f, red_b, status);
     {
-      const D1Epi ep = d1_epi(__ldg(&Lw.sq), __ldg(&Lw.sk), __ldg(&Lw.sv), qd, qd + kvd, am);
+      const D1Epi ep = d1_epi(l_sq, l_sk, l_sv, qd, qd + kvd, am);
       if (!slot_wait(0, l)) break;
       d1_gemv_any(sm_s + P.slot_off[0], nr[0], kw4[0], xs, ep, r0[0], P.qkv, nullptr);
     }
@@ -774,8 +838,7 @@ __global__ void __launch_bounds__(kD1Threads, 1)
     load_row(v, row, P.attn, qd);
     am = d1_norm_quant(v, wv, row, qd, P.eps, xq, kw4[1] * 64, &s_bc, red_f, red_b, status);
     {
-      const float so = __ldg(&Lw.so);
-      const D1Epi ep = d1_epi(so, so, so, H, H, am);
+      const D1Epi ep = d1_epi(l_so, l_so, l_so, H, H, am);
       if (!slot_wait(1, l)) break;
       d1_gemv_any(sm_s + P.slot_off[1], nr[1], kw4[1], xs, ep, r0[1], P.h, hown);
     }
@@ -787,8 +850,7 @@ __global__ void __launch_bounds__(kD1Threads, 1)
     load_row(v, row, P.h, H);
     am = d1_norm_quant(v, wv, row, H, P.eps, xq, kw4[2] * 64, &s_bc, red_f, red_b, status);
     {
-      const float su = __ldg(&Lw.su);
-      const D1Epi ep = d1_epi(__ldg(&Lw.sg), su, su, F, 2 * F, am);
+      const D1Epi ep = d1_epi(l_sg, l_su, l_su, F, 2 * F, am);
       if (!slot_wait(2, l)) break;
       d1_gemv_any(sm_s + P.slot_off[2], nr[2], kw4[2], xs, ep, r0[2], P.gu, nullptr);
     }
@@ -799,8 +861,7 @@ __global__ void __launch_bounds__(kD1Threads, 1)
     load_gate_up(v, row, P.gu, F);
     am = d1_norm_quant(v, wv, row, F, P.eps, xq, kw4[3] * 64, &s_bc, red_f, red_b, status);
     {
-      const float sd = __ldg(&Lw.sd);
-      const D1Epi ep = d1_epi(sd, sd, sd, H, H, am);
+      const D1Epi ep = d1_epi(l_sd, l_sd, l_sd, H, H, am);
       if (!slot_wait(3, l)) break;
       d1_gemv_any(sm_s + P.slot_off[3], nr[3], kw4[3], xs, ep, r0[3], P.h, hown);
     }
