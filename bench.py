@@ -22,7 +22,9 @@ next-token ids out to host every step).  The same line carries:
 * `strong` (N > 1): the N = 1 workload's 256 sequences split over the ranks;
 * `c5` (N > 1): the scaled model tensor-parallel over the ranks;
 * `c2` (N = 1): the ternary matmul op sweep, M in {1, 8, 64, 512, 4096};
-* `gemv_m1`, `batch1`, `prefill` (C3), per-kernel-class times.
+* `gemv_m1` (one layer's single-row GEMVs), `gemv_stream` (the same GEMV
+  over all layers' weights of one input width, one launch), `batch1`,
+  `prefill` (C3), per-kernel-class times.
 
 `--impl reference` times the CPU restatement of the reference backend
 (oracle/) on the host cores.
@@ -218,6 +220,69 @@ def gemv_sweep(backend, dev, peak_gbs, min_bytes=320e6):
             lib.bitnet_cuda_weight_destroy(h)
     out["per_layer"] = {"us": round(tot_ms * 1e3, 3), "gbs": round(tot_b / (tot_ms / 1e3) / 1e9, 1),
                         "frac": round(tot_b / (tot_ms / 1e3) / 1e9 / peak_gbs, 3)}
+    return out
+
+
+# The same single-row GEMV over every layer's weights of one input width at
+# once: all 30 layers' qkv, o and gate/up rows (K = 2560) as one matrix, and
+# all 30 down projections (K = 6912).  One launch streams 388 MB or 133 MB
+# (> 2x L2), so it shows the kernel's HBM rate without the per-launch latency
+# that bounds a single 1.6-8.8 MB projection.
+GEMV_STREAM = [("all_k2560", 30 * (3840 + 2560 + 13824), 2560), ("all_down", 30 * 2560, 6912)]
+
+
+def gemv_stream(backend, dev, peak_gbs, reps=8):
+    import ctypes as C
+
+    import torch
+
+    from bitnetrs_b200 import _native as N
+    from bitnetrs_b200 import synth
+
+    lib = N.cuda_lib()
+    out = {}
+    for name, n, k in GEMV_STREAM:
+        packed = synth.ternary_codes(SEED, 23, n, k)
+        h = C.c_void_p()
+        N.check(lib.bitnet_cuda_weight_upload(backend.handle, packed.ctypes.data, packed.size, n, k, 0.02,
+                                              C.byref(h)))
+        del packed
+        ldq = (k + 63) // 64 * 64
+        xb = synth.bf16_normal(SEED, 24, k, 1.0)
+        d_x = torch.from_numpy(xb.view(np.int16).copy()).to(dev)
+        d_xq = torch.zeros(ldq, dtype=torch.int8, device=dev)
+        d_amax = torch.zeros(1, dtype=torch.float32, device=dev)
+        d_rs = torch.zeros(1, dtype=torch.int32, device=dev)
+        d_st = torch.zeros(1, dtype=torch.int32, device=dev)
+        d_out = torch.zeros(n, dtype=torch.float32, device=dev)
+        s = torch.cuda.Stream(device=dev)
+        torch.cuda.synchronize()
+        N.check(lib.bitnet_cuda_quantize_rows_device(backend.handle, d_x.data_ptr(), 1, 1, k, d_xq.data_ptr(), ldq,
+                                                     d_amax.data_ptr(), d_rs.data_ptr(), d_st.data_ptr(),
+                                                     C.c_void_p(s.cuda_stream)))
+
+        def launch():
+            N.check(lib.bitnet_cuda_ternary_matmul_device(backend.handle, h, d_xq.data_ptr(), ldq,
+                                                          d_amax.data_ptr(), d_rs.data_ptr(), 1, d_out.data_ptr(),
+                                                          None, C.c_void_p(s.cuda_stream)))
+
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                launch()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(reps):
+                launch()
+            e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        b = n * k / 4 + k + 4 + 4 * n
+        out[name] = {"N": n, "K": k, "mb": round(b / 1e6, 1), "us_per_launch": round(ms * 1e3, 2),
+                     "gbs": round(b / (ms / 1e3) / 1e9, 1), "frac": round(b / (ms / 1e3) / 1e9 / peak_gbs, 3)}
+        lib.bitnet_cuda_weight_destroy(h)
+        del d_out
     return out
 
 
@@ -675,9 +740,10 @@ def run_cuda(a):
                   "placement": "bitnetrs_b200.dp.shard_requests (longest context first to the least-loaded rank)"}
 
     # ---- decode GEMV sweep (rank 0) ----
-    gemv_m1 = None
+    gemv_m1, gemv_st = None, None
     if rank == 0 and not a.no_gemv_sweep:
         gemv_m1 = gemv_sweep(backend, dev, peak)
+        gemv_st = gemv_stream(backend, dev, peak)
 
     # ---- C2 op sweep (rank 0, N = 1) ----
     c2 = c2_sweep(backend, dev, peak) if rank == 0 and world == 1 and not a.no_c2 else None
@@ -728,6 +794,7 @@ def run_cuda(a):
             "parity": parity,
             "strong": strong,
             "gemv_m1": gemv_m1,
+            "gemv_stream": gemv_st,
             "c2": c2,
             "c5": c5,
             "gemv": {"kernel": "ternary matmul (i2 x i8 -> i32; tcgen05 kind::i8 for the batch-256 step, dp4a GEMV "

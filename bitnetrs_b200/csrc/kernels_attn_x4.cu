@@ -255,20 +255,15 @@ __global__ void __launch_bounds__(kQkThreads, 3) attn_qk_softmax_kernel(
         // sum = ((e_0 + e_1) + e_2) + ... of head tid, loads issued a block ahead
         const float* e = reinterpret_cast<const float*>(e_sm) + tid;
         const int full = len & ~15;
-        float a[16];
+        int i = 0;
+        for (; i < full; i += 16) {
+          float a[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) a[k] = full ? e[4 * k] : 0.0f;
-        for (int i = 0; i < full; i += 16) {
-          float b[16];
-          const int nx = i + 16 < full ? i + 16 : i;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) b[k] = e[4 * (nx + k)];
+          for (int k = 0; k < 16; ++k) a[k] = e[4 * (i + k)];
 #pragma unroll
           for (int k = 0; k < 16; ++k) sum = __fadd_rn(sum, a[k]);
-#pragma unroll
-          for (int k = 0; k < 16; ++k) a[k] = b[k];
         }
-        for (int i = full; i < len; ++i) sum = __fadd_rn(sum, e[4 * i]);
+        for (; i < len; ++i) sum = __fadd_rn(sum, e[4 * i]);
       }
       __syncthreads();
     }

@@ -266,20 +266,23 @@ __global__ void __launch_bounds__(NT) norm_quant_reg_kernel(const float* __restr
     const int chunks = d >> 3;
     float acc = 0.0f;
     if (lane < 8) {
-      const int full = chunks & ~15;
-      float cur[16];
+      // two 16-element register blocks in turn: one block's loads are in
+      // flight while the other's FMAs run, with no register copies in the loop
+      const int full = chunks & ~31;
+      float ba[16], bb[16];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) cur[k] = full ? row[8 * k + lane] : 0.0f;
+      for (int k = 0; k < 16; ++k) ba[k] = full ? row[8 * k + lane] : 0.0f;
       int i = 0;
-      for (; i < full; i += 16) {
-        float nxt[16];
-        const int ni = i + 16 < full ? i + 16 : i;
+      for (; i < full; i += 32) {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) nxt[k] = row[8 * (ni + k) + lane];
+        for (int k = 0; k < 16; ++k) bb[k] = row[8 * (i + 16 + k) + lane];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(cur[k], cur[k], acc);
+        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(ba[k], ba[k], acc);
+        const int ni = i + 32 < full ? i + 32 : i;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
+        for (int k = 0; k < 16; ++k) ba[k] = row[8 * (ni + k) + lane];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = __fmaf_rn(bb[k], bb[k], acc);
       }
       for (; i < chunks; ++i) {
         const float a = row[8 * i + lane];

@@ -96,35 +96,30 @@ __global__ void __launch_bounds__(256) gemv_m1_kernel(const uint32_t* __restrict
 #pragma unroll
   for (int k = 0; k < 8; ++k) xsum += red[k];
   if (row0 >= N) return;
-  int acc[R];
+  int acc[R][4];
 #pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = 0;
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[r][i] = 0;
 #pragma unroll
   for (int j = 0; j < CH; ++j) {
     const int c = lane + 32 * j;
     if (c < kw4) {
       const uint4* x = xs4 + 4 * c;
-      const uint4 x0 = x[0], x1 = x[1], x2 = x[2], x3 = x[3];
+      const uint4 xv[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const uint32_t wv[4] = {w[r][j].x, w[r][j].y, w[r][j].z, w[r][j].w};
-        const uint4 xv[4] = {x0, x1, x2, x3};
-        int d = acc[r];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          d = __dp4a((int)(wv[q] & 0x03030303u), (int)xv[q].x, d);
-          d = __dp4a((int)((wv[q] >> 2) & 0x03030303u), (int)xv[q].y, d);
-          d = __dp4a((int)((wv[q] >> 4) & 0x03030303u), (int)xv[q].z, d);
-          d = __dp4a((int)((wv[q] >> 6) & 0x03030303u), (int)xv[q].w, d);
-        }
-        acc[r] = d;
+        dp4a_word_scaled(w[r][j].x, xv[0], acc[r]);
+        dp4a_word_scaled(w[r][j].y, xv[1], acc[r]);
+        dp4a_word_scaled(w[r][j].z, xv[2], acc[r]);
+        dp4a_word_scaled(w[r][j].w, xv[3], acc[r]);
       }
     }
   }
   const float am = amax[0];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int s = warp_sum_i(acc[r]);
+    const int s = warp_sum_i(codes_sum(acc[r]));
     if (lane == 0 && row0 + r < N) {
       const int n = row0 + r;
       const int32_t a = xsum - s;
@@ -169,16 +164,12 @@ __global__ void __launch_bounds__(128) gemv_m1_long_kernel(const uint32_t* __res
     uint4 w = __ldcs(wp + i);  // streamed once: evict-first
     int r = i / kw4, c = i - r * kw4;
     const uint4* x = xs4 + 4 * c;
-    uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-    int d = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 xv = x[q];
-      d = __dp4a((int)(wv[q] & 0x03030303u), (int)xv.x, d);
-      d = __dp4a((int)((wv[q] >> 2) & 0x03030303u), (int)xv.y, d);
-      d = __dp4a((int)((wv[q] >> 4) & 0x03030303u), (int)xv.z, d);
-      d = __dp4a((int)((wv[q] >> 6) & 0x03030303u), (int)xv.w, d);
-    }
+    int dd[4] = {0, 0, 0, 0};
+    dp4a_word_scaled(w.x, x[0], dd);
+    dp4a_word_scaled(w.y, x[1], dd);
+    dp4a_word_scaled(w.z, x[2], dd);
+    dp4a_word_scaled(w.w, x[3], dd);
+    const int d = codes_sum(dd);
 #pragma unroll
     for (int rr = 0; rr < R; ++rr)
       if (r == rr) acc[rr] += d;

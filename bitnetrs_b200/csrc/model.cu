@@ -364,9 +364,17 @@ int model_wait(bitnet_cuda_model* m, cudaStream_t st) {
       std::string why = late ? "no completion within " + std::to_string(m->tp_timeout_ms) + " ms"
                              : std::string("NCCL error: ") + m->nc->error_string(ae);
       tp_abort(m);
-      cudaStreamSynchronize(st);  // the aborted collectives have returned
+      // the aborted collectives should now return; the wait for them is
+      // bounded too, since a collective that does not observe the abort
+      // would keep the stream busy until the process exits
+      const auto t1 = std::chrono::steady_clock::now();
+      while (cudaStreamQuery(st) == cudaErrorNotReady &&
+             std::chrono::steady_clock::now() - t1 < std::chrono::milliseconds(m->tp_timeout_ms))
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+      const bool idle = cudaStreamQuery(st) != cudaErrorNotReady;
       cudaGetLastError();
-      return backend_error("tensor-parallel step failed (" + why + "); communicator aborted");
+      return backend_error("tensor-parallel step failed (" + why + "); communicator aborted" +
+                           (idle ? std::string() : std::string("; its stream is still busy: end the process")));
     }
     std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
@@ -690,6 +698,13 @@ static void model_release(bitnet_cuda_model* m) {
   bitnet_cuda_ctx* c = m->ctx;
   cudaSetDevice(c->device);
   if (m->tp && model_wait(m, c->stream) != BITNET_OK) cudaGetLastError();
+  if (m->tp_dead && cudaStreamQuery(c->stream) == cudaErrorNotReady) {
+    // an aborted collective never returned: freeing would wait for it
+    // forever, so the device memory stays with the process, which must end
+    cudaGetLastError();
+    delete m;
+    return;
+  }
   cudaStreamSynchronize(c->stream);
   // graphs that hold NCCL calls go before their communicator
   drop_graphs(m);

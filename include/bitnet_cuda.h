@@ -301,7 +301,8 @@ void bitnet_cuda_model_destroy(bitnet_cuda_model* model);
  * rank then calls bitnet_cuda_model_create_tp with those bytes and the FULL
  * host weights (collective: all ranks call it together), and every later
  * forward, prefill and decode step on all ranks together with the same
- * batch.  Tensor-parallel steps launch without CUDA-graph capture.  A
+ * batch.  Tensor-parallel decode steps run as CUDA graphs holding the NCCL
+ * calls (prefill and forward launch eagerly).  A
  * rank's KV cache holds only its KV heads: bitnet_cuda_kv_seq_write / _read
  * take [layer][pos][local_kv_heads*head_dim] with local_kv_heads =
  * num_key_value_heads/world.
