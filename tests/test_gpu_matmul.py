@@ -111,3 +111,43 @@ def test_decode_gemv_bit_exact(cuda_backend, N_, K):
     assert L.orc_ternary_gemv_preq(O.p(packed), packed.size, scale, O.p(np.ascontiguousarray(xq[0])), K,
                                    float(d_amax.item()), O.p(ro), N_, N_, K, None) == 0
     np.testing.assert_array_equal(d_out.cpu().numpy()[0], ro)
+
+
+@pytest.mark.parametrize("N_,K", [(40000, 2560), (38000, 6912), (40001, 2048)])
+def test_decode_gemv_many_rows_bit_exact(cuda_backend, N_, K):
+    """M = 1 over tens of thousands of rows (the shape of the bench's
+    gemv_stream, every layer's weights of one input width in one launch):
+    int32 accumulators and f32 outputs equal to the oracle's
+    ternary_gemv_quantised."""
+    import torch
+
+    lib = N.cuda_lib()
+    dev = torch.device("cuda", cuda_backend.device_id)
+    packed = synth.ternary_codes(N_ + K, 6, N_, K)
+    scale = 0.0117
+    wh = C.c_void_p()
+    N.check(lib.bitnet_cuda_weight_upload(cuda_backend.handle, packed.ctypes.data, packed.size, N_, K, scale,
+                                          C.byref(wh)))
+    ldq = (K + 63) // 64 * 64
+    x_bf16 = synth.bf16_normal(K, 10, K, 1.0)
+    d_x = torch.from_numpy(x_bf16.view(np.int16).copy()).to(dev)
+    d_xq = torch.zeros((1, ldq), dtype=torch.int8, device=dev)
+    d_amax = torch.zeros(1, dtype=torch.float32, device=dev)
+    d_rs = torch.zeros(1, dtype=torch.int32, device=dev)
+    d_st = torch.zeros(1, dtype=torch.int32, device=dev)
+    d_out = torch.zeros((1, N_), dtype=torch.float32, device=dev)
+    d_acc = torch.zeros((1, N_), dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    N.check(lib.bitnet_cuda_quantize_rows_device(cuda_backend.handle, d_x.data_ptr(), 1, 1, K, d_xq.data_ptr(), ldq,
+                                                 d_amax.data_ptr(), d_rs.data_ptr(), d_st.data_ptr(), None))
+    N.check(lib.bitnet_cuda_ternary_matmul_device(cuda_backend.handle, wh, d_xq.data_ptr(), ldq, d_amax.data_ptr(),
+                                                  d_rs.data_ptr(), 1, d_out.data_ptr(), d_acc.data_ptr(), None))
+    torch.cuda.synchronize()
+    lib.bitnet_cuda_weight_destroy(wh)
+    xq = np.ascontiguousarray(d_xq.cpu().numpy()[0, :K])
+    ro = np.zeros(N_, dtype=np.float32)
+    racc = np.zeros(N_, dtype=np.int32)
+    assert L.orc_ternary_gemv_preq(O.p(packed), packed.size, scale, O.p(xq), K, float(d_amax.item()), O.p(ro), N_,
+                                   N_, K, O.p(racc)) == 0
+    np.testing.assert_array_equal(d_acc.cpu().numpy()[0], racc)
+    np.testing.assert_array_equal(d_out.cpu().numpy()[0], ro)
