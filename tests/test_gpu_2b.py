@@ -146,3 +146,30 @@ def test_2b_batch256_decode_sampled_rows(cuda_backend, w2b, oracle2b):
                 assert int(tout[j]) == ref_tok, f"row {i} step {s}: token {tout[j]} vs oracle {ref_tok}"
         del okv
     print("row, context, step, rel |dlogit|, oracle token, gpu token:", report)
+
+
+def test_2b_ragged_prefill_packed(cuda_backend, w2b, oracle2b):
+    """C3 as bench.py runs it, at a size the oracle finishes in seconds: five
+    seeded prompts of lengths U[32, 300] packed into steps of at most 512
+    tokens (bitnetrs_b200.batching.pack_steps; a prompt continues in the next
+    step), bf16 paged cache, default numerics (tcgen05 GEMM at M up to 512,
+    reference-order causal attention).  Each prompt's last logits and greedy
+    token must equal the oracle's forward over the same prompt: fewer than 17
+    output rows per step keep the lm_head in reference order, so the logits
+    are bit-identical."""
+    cfg = w2b.config
+    lens = synth.uniform_u32(0, 21, 5, 32, 300).astype(int).tolist()
+    prompts = [synth.uniform_u32(0, 100 + s, n, 0, cfg.vocab_size - 1) for s, n in enumerate(lens)]
+    m = BitNetModel(w2b, cuda_backend, max_batch_tokens=512)
+    kv = m.new_kv_cache(num_pages=sum((n + 15) // 16 for n in lens) + 16, max_seqs=len(lens), kv_dtype=KV_BF16)
+    nxt, logits = m.prefill_packed(kv, list(range(len(lens))), prompts, want_logits=True)
+    kv.close()
+    m.close()
+    assert sum(lens) > 512  # at least two steps, one prompt split across them
+    L = O.lib()
+    for i, p in enumerate(prompts):
+        okv = oracle2b.kv(lens[i] + 4, bf16=True)
+        r = oracle2b.forward(okv, p.tolist(), 0)
+        np.testing.assert_array_equal(logits[i], r, err_msg=f"prompt {i} (length {lens[i]})")
+        assert int(nxt[i]) == int(L.orc_greedy_argmax(O.p(r), r.size))
+        del okv
