@@ -758,7 +758,11 @@ def run_cuda(a):
     c5 = None
     if world > 1 and not a.no_c5:
         weights = None  # the 2B host weights are not needed past this point at N > 1
-        c5 = c5_measure(a, dist, world, rank, local, dev)
+        try:
+            c5 = c5_measure(a, dist, world, rank, local, dev)
+        except Exception as e:  # reported in the line; the C4 measurement above stands
+            print(f"[bench] C5 failed on rank {rank}: {e!r}", file=sys.stderr, flush=True)
+            c5 = {"error": repr(e)} if rank == 0 else None
 
     # ---- CPU baseline and parity of the sampled rows (rank 0, N = 1) ----
     cpu, parity = None, None
