@@ -151,3 +151,16 @@ def test_decode_gemv_many_rows_bit_exact(cuda_backend, N_, K):
                                    N_, K, O.p(racc)) == 0
     np.testing.assert_array_equal(d_acc.cpu().numpy()[0], racc)
     np.testing.assert_array_equal(d_out.cpu().numpy()[0], ro)
+
+
+# The per-rank projection shapes of the scaled model split over 2, 4 and 8
+# tensor-parallel ranks (q/k/v and gate/up by rows, o and down by columns),
+# at the decode batch of C5 and at one row.
+TP_SHAPES = sorted({(N_, K) for w in (2, 4, 8) for N_, K in (
+    ((32 // w + 2 * (8 // w)) * 128, 4096), (4096, 32 // w * 128), (2 * 14336 // w, 4096), (4096, 14336 // w))})
+
+
+@pytest.mark.parametrize("M", [1, 64])
+@pytest.mark.parametrize("N_,K", TP_SHAPES)
+def test_device_matmul_tp_rank_shapes(cuda_backend, M, N_, K):
+    test_device_matmul_bit_exact(cuda_backend, M, N_, K)
