@@ -707,7 +707,7 @@ def run_cuda(a):
     torch.cuda.synchronize()
     kt1 = model.kernel_times()
     model.set_kernel_timing(False)
-    per_tok = 521011200 + 328335360 + 513024 + 76800 * 160 + 5120  # SURVEY 8(d) C1 bytes per token at context 160
+    per_tok = 521011200 + 328335360 + 513024 + 76800 * 160 + 5120  # per token at context 160: ternary weights, i8 lm_head + scales, bf16 KV read, embedding row
     b1 = {"value": 1e3 / b1_ms, "unit": "tokens/s", "ms_per_token": b1_ms, "context": "128..160",
           "hbm_gbs": per_tok / (b1_ms / 1e3) / 1e9, "frac": per_tok / (b1_ms / 1e3) / 1e9 / peak,
           "kernels_ms_per_token": {k: round(v[0], 4) for k, v in kt1.items()},
